@@ -1,0 +1,307 @@
+"""Benchmark of the DSA sparse-attention decode path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl {ours,reference}]
+
+Workload (BASELINE cfg2, synthetic, seeded): per GPU one decode batch of
+T=64 query tokens, 16 heads, contexts U[1024, 65536], page size 64, shuffled
+page tables, 2048 distinct top-k positions per token (-1 padded), bf16
+~N(0,1) queries, ~N(0,0.25) latent cache (about 2.3 GB per GPU).  A step is
+one call of the operator over the batch.  Under torchrun each rank runs its
+own batch (request sharding, no collective on the data path; weak scaling).
+
+Metric: query tokens per second, whole job (all ranks); also reported as
+achieved HBM GB/s of the attention kernel against MEASURED_PEAKS.json.
+L2 is flushed (256 MiB write) before every timed step; each step is timed
+with CUDA events on the launching stream and summed, max over ranks.
+
+--impl reference times the reference algorithm on the host cores instead:
+the CPU port of the reference golden function (oracle/, the reference
+itself is Python and cannot be installed on the GPU box), rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "DSA decode query-tokens/sec (whole job); achieved HBM GB/s vs B200 peak"
+UNIT = "query_tokens/s"
+WORKLOAD = ("cfg2 batched decode: T=64 tokens/GPU, 16 heads, ckv512+kpe64 bf16, page 64, "
+            "ctx U[1024,65536], topk 2048 (-1 padded), shuffled page tables")
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks + throttle reasons sampled during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index),
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 7:
+                try:
+                    rows.append((float(f[0]), float(f[1]), f[3:7]))
+                except ValueError:
+                    pass
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v == "Active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def dist_setup(n):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n and world != 1:
+        raise SystemExit(f"--gpus {n} but WORLD_SIZE={world}")
+    return rank, world, local
+
+
+def cpu_baseline_run(qn, qp, ckv, kpe, idx, scale, reps=3):
+    """The reference algorithm (CPU port in oracle/) on the rows of the same
+    batch: the selected rows are compacted into a small host cache so the
+    work per token is identical.  Returns (tokens/s, cores, sample)."""
+    from oracle import oracle as O
+
+    def out_bits(t):
+        return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+    valid = idx >= 0
+    uniq, inv = torch.unique(idx[valid].long(), return_inverse=True)
+    sidx = torch.full_like(idx, -1)
+    sidx[valid] = inv.to(torch.int32)
+    npg = (uniq.numel() + 63) // 64
+
+    def compact(cache, d):
+        flat = cache.reshape(-1, d)[uniq]
+        pad = torch.zeros((npg * 64 - uniq.numel(), d), dtype=cache.dtype, device=cache.device)
+        return out_bits(torch.cat([flat, pad]).reshape(npg, 64, d))
+
+    args = (out_bits(qn), out_bits(qp), compact(ckv, 512), compact(kpe, 64), sidx.cpu().numpy())
+    cores = os.cpu_count() or 1
+    O.dsa_attention(*args, scale, nthreads=cores)  # warm-up
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        O.dsa_attention(*args, scale, nthreads=cores)
+        times.append(time.perf_counter() - t0)
+    T = idx.shape[0]
+    return T / statistics.median(times), cores, (
+        f"full batch of {T} tokens (selected rows compacted to host), median of {reps}")
+
+
+def run_reference_arm(args):
+    rank, world, local = dist_setup(args.gpus)
+    if rank != 0:
+        return
+    from flashinfer_repo_b200.bench_inputs import make_cfg2_device
+    dev = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
+    qn, qp, ckv, kpe, idx, scale = make_cfg2_device(seed=0, device=dev)
+    vals = []
+    for i in range(args.warmup + args.steps):
+        v, cores, sample = cpu_baseline_run(qn, qp, ckv, kpe, idx, scale, reps=1)
+        if i >= args.warmup:
+            vals.append(v)
+    v = statistics.median(vals)
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * idx.shape[0] / v,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic (seeded, BASELINE cfg2 shapes and distributions)",
+        "config": {"workload": WORKLOAD, "tokens_per_gpu": int(idx.shape[0]),
+                   "note": "reference arm: CPU port of the reference golden function "
+                           "(solution/triton/indexer_kernel.py:436-497) on all host cores; the "
+                           "reference has no installable package"},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_ours(args):
+    rank, world, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    from flashinfer_repo_b200 import kernel, read_device_error
+    from flashinfer_repo_b200.bench_inputs import attention_bytes, make_cfg2_device
+
+    qn, qp, ckv, kpe, idx, scale = make_cfg2_device(seed=1000 + rank, device=dev)
+    T = idx.shape[0]
+    alg_bytes = attention_bytes(idx)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    out = torch.empty((T, 16, 512), dtype=torch.bfloat16, device=dev)
+    lse = torch.empty((T, 16), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    for _ in range(args.warmup):
+        flush.fill_(1)
+        kernel(qn, qp, ckv, kpe, idx, scale, output=out, lse=lse)
+    torch.cuda.synchronize()
+    if read_device_error(dev):
+        raise SystemExit("device error flag set during warm-up")
+
+    # ---- device-resident timing (value + roofline): one kernel launch per step
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            starts[i].record(stream)
+            kernel(qn, qp, ckv, kpe, idx, scale, output=out, lse=lse)
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = sum(step_ms)
+    clocks = clk.summary()
+
+    # ---- end to end through the public API with host buffers
+    h_qn = qn.cpu().pin_memory()
+    h_qp = qp.cpu().pin_memory()
+    h_idx = idx.cpu().pin_memory()
+    h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    h_lse = torch.empty(lse.shape, dtype=lse.dtype).pin_memory()
+    d_qn, d_qp, d_idx = torch.empty_like(qn), torch.empty_like(qp), torch.empty_like(idx)
+    h2d = h_qn.numel() * 2 + h_qp.numel() * 2 + h_idx.numel() * 4
+    d2h = h_out.numel() * 2 + h_lse.numel() * 4
+
+    def e2e_step():
+        d_qn.copy_(h_qn, non_blocking=True)
+        d_qp.copy_(h_qp, non_blocking=True)
+        d_idx.copy_(h_idx, non_blocking=True)
+        o, l = kernel(d_qn, d_qp, ckv, kpe, d_idx, scale)
+        h_out.copy_(o, non_blocking=True)
+        h_lse.copy_(l, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    e_ms = []
+    for i in range(args.steps):
+        flush.fill_(i & 0xFF)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        e2e_step()
+        e.record(stream)
+        e.synchronize()
+        e_ms.append(s.elapsed_time(e))
+    e2e_total = sum(e_ms)
+    if read_device_error(dev):
+        raise SystemExit("device error flag set during the timed steps")
+
+    # max over ranks
+    t = torch.tensor([total_ms, e2e_total], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, e2e_total = t.tolist()
+    value = world * T * args.steps / (total_ms / 1e3)
+    e2e_value = world * T * args.steps / (e2e_total / 1e3)
+    avg_kernel_ms = statistics.mean(step_ms)
+    achieved = alg_bytes / (avg_kernel_ms / 1e3) / 1e9
+    peak, peak_kind = peaks()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, cores, sample = cpu_baseline_run(qn, qp, ckv, kpe, idx, scale)
+        cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded, BASELINE cfg2 shapes and distributions)",
+            "config": {"workload": WORKLOAD, "tokens_per_gpu": T, "parallelism": f"request-shard x{world}",
+                       "l2": "flushed before every step (256 MiB write, untimed)",
+                       "alg_bytes_per_step_per_gpu": alg_bytes},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
+                         "kernel": "dsa_attention_kernel", "avg_kernel_ms": avg_kernel_ms},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }), flush=True)
+    if dist:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,69 @@
+"""ctypes binding of libdsa_b200.so (the C ABI declared in include/dsa_b200.h).
+
+The library is built in-tree by flashinfer_repo_b200.build.  There is no
+fallback: if the library is missing or a call fails, an exception is raised.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+from . import build as _build
+
+_lib = None
+
+I64 = ctypes.c_int64
+P = ctypes.c_void_p
+SZ = ctypes.c_size_t
+F32 = ctypes.c_float
+INT = ctypes.c_int
+
+# name -> argtypes; every function returns int (dsa_status) except the message.
+SIGNATURES = {
+    "dsa_sparse_attention_workspace_size": [I64, I64, I64, ctypes.POINTER(SZ)],
+    "dsa_sparse_attention": [P, I64, I64, P, I64, I64, P, I64, I64, P, I64, I64, P, I64,
+                             I64, I64, I64, I64, I64, F32, P, I64, I64, P, I64, I64, P, SZ, P],
+    "dsa_read_device_error": [P, INT, ctypes.POINTER(INT), P],
+}
+
+
+class DSAError(RuntimeError):
+    """A failing call of the native library (status code + message)."""
+
+    def __init__(self, fn, code, msg):
+        super().__init__(f"{fn} failed with status {code}: {msg}")
+        self.code = code
+
+
+def lib_path() -> str:
+    return _build.LIB
+
+
+def load(build_if_missing: bool = True):
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = lib_path()
+    if not os.path.exists(path):
+        if not build_if_missing:
+            raise OSError(f"{path} is missing; run python -m flashinfer_repo_b200.build")
+        _build.build()
+    lib = ctypes.CDLL(path)
+    lib.dsa_last_error_message.restype = ctypes.c_char_p
+    lib.dsa_last_error_message.argtypes = []
+    for name, args in SIGNATURES.items():
+        f = getattr(lib, name)
+        f.argtypes = args
+        f.restype = INT
+    _lib = lib
+    return lib
+
+
+def check(fn_name: str, rc: int):
+    if rc != 0:
+        msg = load().dsa_last_error_message().decode(errors="replace")
+        raise DSAError(fn_name, rc, msg)
+
+
+def call(fn_name: str, *args):
+    check(fn_name, getattr(load(), fn_name)(*args))

@@ -1,0 +1,662 @@
+// attention.cu -- DSA sparse-attention decode over a paged MLA latent cache, sm_100a.
+//
+// Semantics follow the reference operator `kernel` / `dsa_fwd_kernel`
+// (solution/triton/kernel.py:9-182) and its split-K variant
+// (kernel.py:343-567):  for every query token and each of its 16 heads,
+//   s_j   = (q_nope . ckv[row_j] + q_pe . kpe[row_j]) * sm_scale  over the
+//           top-k rows (row = flat slot id page*64+offset, -1 = padding)
+//   out   = softmax(s) . ckv[rows]      (bf16; 0 when no row is valid)
+//   lse   = log2(sum_j exp(s_j))         (fp32, base 2; -inf when no row)
+// P is rounded to bf16 before the PV product, as in the reference (:114).
+//
+// Design (B200):
+//  * Work unit = tile of 32 selected rows of one (token, 16-head group).
+//    A token's 2048 rows are 64 tiles; the whole batch is one list of tiles
+//    split evenly over a persistent grid (one contiguous range per CTA), so
+//    any T keeps every SM streaming (stream-K over the top-k dimension).
+//  * A producer warp turns indices into row addresses and gathers each
+//    1024-B ckv row and 128-B kpe row with one cp.async.bulk each into a
+//    padded shared-memory ring (row pitch 1040 / 144 B: conflict-free
+//    ldmatrix), completion tracked by mbarrier transaction bytes.
+//  * Four consumer warps: QK^T with bf16 tensor-core MMA, the 576-d
+//    contraction split in four 144-d quarters (Q fragments stay in
+//    registers), partial scores reduced through shared memory; online
+//    softmax in registers (base-2, exp2); PV with each warp owning 128 of
+//    the 512 output columns; P is re-used from registers as the A operand.
+//  * A token split across CTAs writes unnormalised (acc, m, l) partials; the
+//    CTA that arrives last on the token's counter merges them (LSE merge of
+//    kernel.py:437-493) in the same launch.  Counters return to zero.
+#include <cstdio>
+#include <cstdlib>
+#include <mutex>
+
+#include "../../include/dsa_b200.h"
+#include "common.cuh"
+
+namespace dsa {
+
+constexpr int kHeads = 16;
+constexpr int kDc = 512;
+constexpr int kDp = 64;
+constexpr int kRows = 32;             // rows per tile
+constexpr int kCkvStride = 1040;      // smem pitch of a 1024-B ckv row
+constexpr int kKpeStride = 144;       // smem pitch of a 128-B kpe row
+constexpr int kCWarps = 4;            // consumer warps
+constexpr int kThreads = (kCWarps + 1) * 32;
+constexpr int kPartFloats = kHeads * kDc + 2 * kHeads;  // acc[16][512], m[16], l[16]
+
+struct AttnParams {
+  const __nv_bfloat16* q_nope;
+  const __nv_bfloat16* q_pe;
+  const __nv_bfloat16* ckv;
+  const __nv_bfloat16* kpe;
+  const int32_t* idx;
+  __nv_bfloat16* out;
+  float* lse;
+  int64_t qn_st, qn_sh, qp_st, qp_sh;  // element strides (token, head)
+  int64_t ckv_sp, ckv_sr, kpe_sp, kpe_sr;  // (page, row)
+  int64_t idx_st;
+  int64_t out_st, out_sh, lse_st, lse_sh;
+  int64_t num_slots;
+  int head_groups;      // heads / 16; virtual token v = t * head_groups + group
+  int tiles_per_token;  // topk / 32
+  float scale_log2;     // sm_scale * log2(e)
+  int tiles_base, tiles_rem, max_seg;
+  float* part;
+  int* counters;
+  int* err;
+};
+
+template <int NST>
+struct AttnSmem {
+  uint8_t ckv[NST][kRows * kCkvStride];
+  uint8_t kpe[NST][kRows * kKpeStride];
+  float4 sred[2][kCWarps][32][4];
+  uint32_t vmask[NST];
+  uint64_t full[NST];
+  uint64_t empty[NST];
+  int last_flag;
+};
+
+__device__ __forceinline__ int cta_start(const AttnParams& p, int c) {
+  return c * p.tiles_base + min(c, p.tiles_rem);
+}
+__device__ __forceinline__ int cta_of_tile(const AttnParams& p, int tile) {
+  const int big = (p.tiles_base + 1) * p.tiles_rem;
+  return tile < big ? tile / (p.tiles_base + 1) : p.tiles_rem + (tile - big) / p.tiles_base;
+}
+__device__ __forceinline__ float* part_slot(const AttnParams& p, int c, int v) {
+  const int j = v - cta_start(p, c) / p.tiles_per_token;
+  return p.part + (int64_t)(c * p.max_seg + j) * kPartFloats;
+}
+
+// ------------------------------------------------------------------ producer
+template <int NST>
+__device__ __forceinline__ void attn_producer(const AttnParams& p, AttnSmem<NST>& S, int lane,
+                                              int tile_begin, int tile_end) {
+  int it = 0;
+  for (int tile = tile_begin; tile < tile_end; ++tile, ++it) {
+    const int s = it % NST;
+    const uint32_t ph = (it / NST) & 1;
+    if (!mbar_wait(&S.empty[s], ph ^ 1)) {
+      set_error(p.err, kErrTimeout);
+      break;
+    }
+    const int v = tile / p.tiles_per_token;
+    const int t = v / p.head_groups;
+    const int r0 = (tile - v * p.tiles_per_token) * kRows;
+    const int32_t id = __ldg(p.idx + (int64_t)t * p.idx_st + r0 + lane);
+    const bool valid = id >= 0 && id < p.num_slots;
+    if (id < -1 || id >= p.num_slots) set_error(p.err, kErrBadIndex);
+    const uint32_t mask = __ballot_sync(0xffffffffu, valid);
+    if (!valid) {
+      // padding row: zeros, so 0-probability rows contribute exactly 0 to PV
+      float4* d = reinterpret_cast<float4*>(S.ckv[s] + lane * kCkvStride);
+#pragma unroll 8
+      for (int k = 0; k < 64; ++k) d[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      float4* e = reinterpret_cast<float4*>(S.kpe[s] + lane * kKpeStride);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) e[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      fence_proxy_async_smem();
+    }
+    if (lane == 0) S.vmask[s] = mask;
+    __syncwarp();
+    if (lane == 0) mbar_arrive_expect_tx(&S.full[s], __popc(mask) * (kDc * 2 + kDp * 2));
+    __syncwarp();
+    if (valid) {
+      const int64_t page = id >> 6, r = id & 63;
+      bulk_g2s(S.ckv[s] + lane * kCkvStride, p.ckv + page * p.ckv_sp + r * p.ckv_sr, kDc * 2,
+               &S.full[s]);
+      bulk_g2s(S.kpe[s] + lane * kKpeStride, p.kpe + page * p.kpe_sp + r * p.kpe_sr, kDp * 2,
+               &S.full[s]);
+    }
+  }
+  // Do not leave while copies issued by this warp may still be landing.
+  for (int k = it > NST ? it - NST : 0; k < it; ++k) mbar_wait(&S.full[k % NST], (k / NST) & 1);
+}
+
+// ------------------------------------------------------------------ merge
+// LSE merge of the partial (acc, m, l) of every CTA that worked on virtual
+// token v (kernel.py:437-493), done by the 128 consumer threads of the CTA
+// that finished last.  Thread i owns output columns 4i..4i+3 of all 16 heads.
+__device__ __noinline__ void attn_merge(const AttnParams& p, int v, int c_first, int c_last) {
+  const int i = threadIdx.x;  // 0..127
+  float M[kHeads], L[kHeads];
+#pragma unroll
+  for (int h = 0; h < kHeads; ++h) {
+    M[h] = -INFINITY;
+    L[h] = 0.f;
+  }
+  for (int c = c_first; c <= c_last; ++c) {
+    const float* pm = part_slot(p, c, v) + kHeads * kDc;
+#pragma unroll
+    for (int h = 0; h < kHeads; ++h) M[h] = fmaxf(M[h], __ldcg(pm + h));
+  }
+  float4 acc[kHeads];
+#pragma unroll
+  for (int h = 0; h < kHeads; ++h) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int c = c_first; c <= c_last; ++c) {
+    const float* ps = part_slot(p, c, v);
+#pragma unroll
+    for (int h = 0; h < kHeads; ++h) {
+      const float m = __ldcg(ps + kHeads * kDc + h);
+      const float l = __ldcg(ps + kHeads * kDc + kHeads + h);
+      const float w = (m == -INFINITY) ? 0.f : exp2f(m - M[h]);
+      L[h] += w * l;
+      const float4 a = __ldcg(reinterpret_cast<const float4*>(ps + h * kDc) + i);
+      acc[h].x += w * a.x;
+      acc[h].y += w * a.y;
+      acc[h].z += w * a.z;
+      acc[h].w += w * a.w;
+    }
+  }
+  const int t = v / p.head_groups, grp = v - t * p.head_groups;
+#pragma unroll
+  for (int h = 0; h < kHeads; ++h) {
+    const float inv = (M[h] == -INFINITY) ? 0.f : 1.f / L[h];
+    uint2 pk;
+    pk.x = pack_bf16(acc[h].x * inv, acc[h].y * inv);
+    pk.y = pack_bf16(acc[h].z * inv, acc[h].w * inv);
+    *reinterpret_cast<uint2*>(p.out + t * p.out_st + (int64_t)(grp * kHeads + h) * p.out_sh +
+                              4 * i) = pk;
+  }
+  if (i < kHeads) {
+    float m = M[0], l = L[0];
+#pragma unroll
+    for (int h = 1; h < kHeads; ++h)
+      if (h == i) {
+        m = M[h];
+        l = L[h];
+      }
+    p.lse[t * p.lse_st + (int64_t)(grp * kHeads + i) * p.lse_sh] =
+        (m == -INFINITY) ? -INFINITY : m + log2f(l);
+  }
+}
+
+// ------------------------------------------------------------------ kernel
+template <int NST>
+__global__ void __launch_bounds__(kThreads, (NST == 2 ? 2 : 1)) dsa_attention_kernel(const __grid_constant__ AttnParams p) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  AttnSmem<NST>& S = *reinterpret_cast<AttnSmem<NST>*>(smem_raw);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cta = blockIdx.x;
+  const int tile_begin = cta_start(p, cta), tile_end = cta_start(p, cta + 1);
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&S.full[s], 1);
+      mbar_init(&S.empty[s], kCWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kCWarps) {
+    attn_producer<NST>(p, S, lane, tile_begin, tile_end);
+    return;
+  }
+
+  // ---------------------------------------------------------------- consumers
+  const int g = lane >> 2, c = lane & 3;
+  const int kq0 = warp * 144;  // this warp's quarter of the 576-d contraction
+  const int tpt = p.tiles_per_token;
+  int it = 0, buf = 0;
+  int tile = tile_begin;
+  while (tile < tile_end) {
+    const int v = tile / tpt;
+    const int seg_end = min(tile_end, (v + 1) * tpt);
+    const int t = v / p.head_groups, grp = v - t * p.head_groups;
+
+    // Q A-fragments for k-steps kq0 + 16j (m16n8k16 row-major A layout).
+    uint32_t qa[9][4];
+    {
+      const __nv_bfloat16* qn = p.q_nope + t * p.qn_st + (int64_t)grp * kHeads * p.qn_sh;
+      const __nv_bfloat16* qp = p.q_pe + t * p.qp_st + (int64_t)grp * kHeads * p.qp_sh;
+#pragma unroll
+      for (int j = 0; j < 9; ++j) {
+        const int kk = kq0 + 16 * j;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int h = g + ((e & 1) ? 8 : 0);
+          const int d = kk + 2 * c + ((e & 2) ? 8 : 0);
+          const __nv_bfloat16* src = d < kDc ? qn + h * p.qn_sh + d : qp + h * p.qp_sh + (d - kDc);
+          qa[j][e] = __ldg(reinterpret_cast<const unsigned int*>(src));
+        }
+      }
+    }
+
+    float o[16][4];
+#pragma unroll
+    for (int nb = 0; nb < 16; ++nb) o[nb][0] = o[nb][1] = o[nb][2] = o[nb][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    bool ok = true;
+
+    for (; tile < seg_end; ++tile, ++it) {
+      const int s = it % NST;
+      if (!mbar_wait(&S.full[s], (it / NST) & 1)) {
+        set_error(p.err, kErrTimeout);
+        ok = false;
+        break;
+      }
+      const uint32_t ckv_base = smem_u32(S.ckv[s]);
+      const uint32_t kpe_base = smem_u32(S.kpe[s]);
+
+      // ---- partial scores over this warp's 144 dims: [16 heads x 32 rows]
+      float sc[4][4];
+#pragma unroll
+      for (int nb = 0; nb < 4; ++nb) sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
+#pragma unroll
+      for (int j = 0; j < 9; ++j) {
+        const int kk = kq0 + 16 * j;
+#pragma unroll
+        for (int pr = 0; pr < 2; ++pr) {
+          const int mi = lane >> 3;
+          const int row = (pr * 2 + (mi >> 1)) * 8 + (lane & 7);
+          const int kc = kk + (mi & 1) * 8;
+          const uint32_t addr = kc < kDc ? ckv_base + row * kCkvStride + kc * 2
+                                         : kpe_base + row * kKpeStride + (kc - kDc) * 2;
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(addr, b0, b1, b2, b3);
+          mma_bf16_16816(sc[pr * 2], qa[j], b0, b1);
+          mma_bf16_16816(sc[pr * 2 + 1], qa[j], b2, b3);
+        }
+      }
+#pragma unroll
+      for (int nb = 0; nb < 4; ++nb)
+        S.sred[buf][warp][lane][nb] = make_float4(sc[nb][0], sc[nb][1], sc[nb][2], sc[nb][3]);
+      named_bar_sync(1, kCWarps * 32);
+      float x[4][4];
+#pragma unroll
+      for (int nb = 0; nb < 4; ++nb) x[nb][0] = x[nb][1] = x[nb][2] = x[nb][3] = 0.f;
+#pragma unroll
+      for (int w = 0; w < kCWarps; ++w) {
+#pragma unroll
+        for (int nb = 0; nb < 4; ++nb) {
+          const float4 a = S.sred[buf][w][lane][nb];
+          x[nb][0] += a.x;
+          x[nb][1] += a.y;
+          x[nb][2] += a.z;
+          x[nb][3] += a.w;
+        }
+      }
+      buf ^= 1;
+
+      // ---- online softmax (base 2), rows g and g+8
+      const uint32_t vm = S.vmask[s];
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int nb = 0; nb < 4; ++nb) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int col = nb * 8 + 2 * c + (e & 1);
+          x[nb][e] = ((vm >> col) & 1u) ? x[nb][e] * p.scale_log2 : -INFINITY;
+        }
+        mx0 = fmaxf(mx0, fmaxf(x[nb][0], x[nb][1]));
+        mx1 = fmaxf(mx1, fmaxf(x[nb][2], x[nb][3]));
+      }
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+      const float a0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - n0);
+      const float a1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - n1);
+      m0 = n0;
+      m1 = n1;
+      float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+      for (int nb = 0; nb < 4; ++nb) {
+        x[nb][0] = (n0 == -INFINITY) ? 0.f : exp2f(x[nb][0] - n0);
+        x[nb][1] = (n0 == -INFINITY) ? 0.f : exp2f(x[nb][1] - n0);
+        x[nb][2] = (n1 == -INFINITY) ? 0.f : exp2f(x[nb][2] - n1);
+        x[nb][3] = (n1 == -INFINITY) ? 0.f : exp2f(x[nb][3] - n1);
+        rs0 += x[nb][0] + x[nb][1];
+        rs1 += x[nb][2] + x[nb][3];
+      }
+      l0 = l0 * a0 + rs0;
+      l1 = l1 * a1 + rs1;
+#pragma unroll
+      for (int nb = 0; nb < 16; ++nb) {
+        o[nb][0] *= a0;
+        o[nb][1] *= a0;
+        o[nb][2] *= a1;
+        o[nb][3] *= a1;
+      }
+      uint32_t pa[2][4];
+#pragma unroll
+      for (int kj = 0; kj < 2; ++kj) {
+        pa[kj][0] = pack_bf16(x[2 * kj][0], x[2 * kj][1]);
+        pa[kj][1] = pack_bf16(x[2 * kj][2], x[2 * kj][3]);
+        pa[kj][2] = pack_bf16(x[2 * kj + 1][0], x[2 * kj + 1][1]);
+        pa[kj][3] = pack_bf16(x[2 * kj + 1][2], x[2 * kj + 1][3]);
+      }
+
+      // ---- PV: this warp's 128 output columns
+#pragma unroll
+      for (int kj = 0; kj < 2; ++kj) {
+#pragma unroll
+        for (int pr = 0; pr < 8; ++pr) {
+          const int mi = lane >> 3;
+          const int row = 16 * kj + (mi & 1) * 8 + (lane & 7);
+          const int col = 128 * warp + 16 * pr + (mi >> 1) * 8;
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(ckv_base + row * kCkvStride + col * 2, b0, b1, b2, b3);
+          mma_bf16_16816(o[2 * pr], pa[kj], b0, b1);
+          mma_bf16_16816(o[2 * pr + 1], pa[kj], b2, b3);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.empty[s]);
+    }
+    if (!ok) break;
+
+    // ---- finish this (token, segment)
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    const int c_first = cta_of_tile(p, v * tpt);
+    const int c_last = cta_of_tile(p, v * tpt + tpt - 1);
+    if (c_first == c_last) {
+      const float i0 = (m0 == -INFINITY) ? 0.f : 1.f / l0;
+      const float i1 = (m1 == -INFINITY) ? 0.f : 1.f / l1;
+      __nv_bfloat16* o0 = p.out + t * p.out_st + (int64_t)(grp * kHeads + g) * p.out_sh;
+      __nv_bfloat16* o1 = o0 + 8 * p.out_sh;
+#pragma unroll
+      for (int nb = 0; nb < 16; ++nb) {
+        const int d = 128 * warp + 8 * nb + 2 * c;
+        *reinterpret_cast<uint32_t*>(o0 + d) = pack_bf16(o[nb][0] * i0, o[nb][1] * i0);
+        *reinterpret_cast<uint32_t*>(o1 + d) = pack_bf16(o[nb][2] * i1, o[nb][3] * i1);
+      }
+      if (warp == 0 && c == 0) {
+        float* lp = p.lse + t * p.lse_st;
+        lp[(int64_t)(grp * kHeads + g) * p.lse_sh] = (m0 == -INFINITY) ? -INFINITY : m0 + log2f(l0);
+        lp[(int64_t)(grp * kHeads + g + 8) * p.lse_sh] =
+            (m1 == -INFINITY) ? -INFINITY : m1 + log2f(l1);
+      }
+    } else {
+      float* ps = part_slot(p, cta, v);
+#pragma unroll
+      for (int nb = 0; nb < 16; ++nb) {
+        const int d = 128 * warp + 8 * nb + 2 * c;
+        __stcg(reinterpret_cast<float2*>(ps + g * kDc + d), make_float2(o[nb][0], o[nb][1]));
+        __stcg(reinterpret_cast<float2*>(ps + (g + 8) * kDc + d), make_float2(o[nb][2], o[nb][3]));
+      }
+      if (warp == 0 && c == 0) {
+        __stcg(ps + kHeads * kDc + g, m0);
+        __stcg(ps + kHeads * kDc + g + 8, m1);
+        __stcg(ps + kHeads * kDc + kHeads + g, l0);
+        __stcg(ps + kHeads * kDc + kHeads + g + 8, l1);
+      }
+      __threadfence();
+      named_bar_sync(1, kCWarps * 32);
+      if (threadIdx.x == 0) {
+        const int old = atomicAdd(p.counters + v, 1);
+        S.last_flag = (old == c_last - c_first);
+      }
+      named_bar_sync(1, kCWarps * 32);
+      if (S.last_flag) {
+        __threadfence();
+        attn_merge(p, v, c_first, c_last);
+        if (threadIdx.x == 0) p.counters[v] = 0;  // leave the counter ready for the next call
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ host side
+namespace {
+
+thread_local char g_errmsg[512] = "";
+
+int fail(int code, const char* msg) {
+  snprintf(g_errmsg, sizeof(g_errmsg), "%s", msg);
+  return code;
+}
+
+struct DevInfo {
+  int sms = 0;
+  int occ[5] = {0, 0, 0, 0, 0};
+};
+std::mutex g_mu;
+DevInfo g_dev[64];
+
+int env_int(const char* name, int dflt) {
+  const char* s = getenv(name);
+  return (s && *s) ? atoi(s) : dflt;
+}
+
+int stages_choice() {
+  const int s = env_int("DSA_ATTN_STAGES", 2);
+  return (s >= 2 && s <= 4) ? s : 2;
+}
+
+template <int NST>
+int smem_bytes() {
+  return (int)sizeof(AttnSmem<NST>);
+}
+
+template <int NST>
+cudaError_t ensure_attr() {
+  return cudaFuncSetAttribute(dsa_attention_kernel<NST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              smem_bytes<NST>());
+}
+
+// SM count and resident CTAs per SM for the given stage count (cached per device).
+int device_slots(int nst, int* sms_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+  std::lock_guard<std::mutex> lk(g_mu);
+  DevInfo& d = g_dev[dev];
+  if (d.sms == 0) {
+    if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return -1;
+  }
+  if (d.occ[nst] == 0) {
+    cudaError_t e;
+    int occ = 0;
+    switch (nst) {
+      case 2:
+        e = ensure_attr<2>();
+        if (e == cudaSuccess)
+          e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, dsa_attention_kernel<2>, kThreads,
+                                                            smem_bytes<2>());
+        break;
+      case 3:
+        e = ensure_attr<3>();
+        if (e == cudaSuccess)
+          e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, dsa_attention_kernel<3>, kThreads,
+                                                            smem_bytes<3>());
+        break;
+      default:
+        e = ensure_attr<4>();
+        if (e == cudaSuccess)
+          e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, dsa_attention_kernel<4>, kThreads,
+                                                            smem_bytes<4>());
+        break;
+    }
+    if (e != cudaSuccess || occ < 1) return -1;
+    d.occ[nst] = occ;
+  }
+  *sms_out = d.sms;
+  return d.occ[nst];
+}
+
+struct Plan {
+  int ctas, base, rem, max_seg;
+  int64_t vtokens, total_tiles;
+  size_t part_off, bytes;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Grid plan: an even split of all tiles over min(slots, tiles/min_tiles) CTAs.
+int make_plan(int64_t num_tokens, int64_t heads, int64_t topk, int nst, Plan* pl) {
+  int sms = 0;
+  const int occ = device_slots(nst, &sms);
+  if (occ < 1) return fail(DSA_ERR_CUDA, "cannot query device / occupancy for the attention kernel");
+  const int64_t tpt = topk / kRows;
+  pl->vtokens = num_tokens * (heads / kHeads);
+  pl->total_tiles = pl->vtokens * tpt;
+  const int min_tiles = env_int("DSA_ATTN_MIN_TILES", 4) > 0 ? env_int("DSA_ATTN_MIN_TILES", 4) : 1;
+  int64_t ctas = (int64_t)sms * occ;
+  const int forced = env_int("DSA_ATTN_CTAS", 0);
+  if (forced > 0) ctas = forced;
+  ctas = std::min<int64_t>(ctas, (pl->total_tiles + min_tiles - 1) / min_tiles);
+  if (ctas < 1) ctas = 1;
+  pl->ctas = (int)ctas;
+  pl->base = (int)(pl->total_tiles / ctas);
+  pl->rem = (int)(pl->total_tiles % ctas);
+  const int64_t longest = pl->base + (pl->rem ? 1 : 0);
+  pl->max_seg = (int)((longest + tpt - 2) / tpt + 1);
+  pl->part_off = align256(256 + 4 * (size_t)pl->vtokens);
+  pl->bytes = pl->part_off + (size_t)pl->ctas * pl->max_seg * kPartFloats * sizeof(float);
+  return DSA_OK;
+}
+
+template <int NST>
+cudaError_t launch(const AttnParams& p, int ctas, cudaStream_t st) {
+  cudaError_t e = ensure_attr<NST>();
+  if (e != cudaSuccess) return e;
+  dsa_attention_kernel<NST><<<ctas, kThreads, smem_bytes<NST>(), st>>>(p);
+  return cudaGetLastError();
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+}  // namespace dsa
+
+using namespace dsa;
+
+extern "C" {
+
+const char* dsa_last_error_message(void) { return g_errmsg; }
+
+int dsa_sparse_attention_workspace_size(int64_t num_tokens, int64_t num_heads, int64_t topk,
+                                        size_t* bytes) {
+  if (!bytes) return fail(DSA_ERR_INVALID_ARG, "bytes is NULL");
+  if (num_tokens < 0 || num_heads <= 0 || num_heads % kHeads || topk <= 0 || topk % kRows)
+    return fail(DSA_ERR_INVALID_ARG, "num_heads must be a multiple of 16 and topk of 32");
+  Plan pl;
+  const int rc = make_plan(num_tokens > 0 ? num_tokens : 1, num_heads, topk, stages_choice(), &pl);
+  if (rc) return rc;
+  *bytes = pl.bytes;
+  return DSA_OK;
+}
+
+int dsa_sparse_attention(const void* q_nope, int64_t q_nope_stride_token, int64_t q_nope_stride_head,
+                         const void* q_pe, int64_t q_pe_stride_token, int64_t q_pe_stride_head,
+                         const void* ckv_cache, int64_t ckv_stride_page, int64_t ckv_stride_row,
+                         const void* kpe_cache, int64_t kpe_stride_page, int64_t kpe_stride_row,
+                         const int32_t* sparse_indices, int64_t indices_stride_token,
+                         int64_t num_tokens, int64_t num_heads, int64_t num_pages, int64_t page_size,
+                         int64_t topk, float sm_scale, void* output, int64_t out_stride_token,
+                         int64_t out_stride_head, float* lse, int64_t lse_stride_token,
+                         int64_t lse_stride_head, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  if (num_tokens < 0) return fail(DSA_ERR_INVALID_ARG, "num_tokens < 0");
+  if (num_heads <= 0 || num_heads % kHeads)
+    return fail(DSA_ERR_UNSUPPORTED, "num_heads must be a positive multiple of 16");
+  if (page_size != 64) return fail(DSA_ERR_UNSUPPORTED, "page_size must be 64");
+  if (topk <= 0 || topk % kRows || topk > (1 << 20))
+    return fail(DSA_ERR_UNSUPPORTED, "topk must be a positive multiple of 32");
+  if (num_pages < 0 || num_pages * 64 > INT32_MAX)
+    return fail(DSA_ERR_INVALID_ARG, "num_pages out of range for int32 slot ids");
+  if (num_tokens == 0) return DSA_OK;
+  if (!q_nope || !q_pe || !ckv_cache || !kpe_cache || !sparse_indices || !output || !lse ||
+      !workspace)
+    return fail(DSA_ERR_INVALID_ARG, "NULL pointer argument");
+  // 16-byte row gathers / fragment loads need aligned rows.
+  if (!aligned16(ckv_cache) || !aligned16(kpe_cache) || ckv_stride_page % 8 || ckv_stride_row % 8 ||
+      kpe_stride_page % 8 || kpe_stride_row % 8)
+    return fail(DSA_ERR_INVALID_ARG, "cache rows must be 16-byte aligned (strides multiple of 8)");
+  if ((reinterpret_cast<uintptr_t>(q_nope) & 3) || (reinterpret_cast<uintptr_t>(q_pe) & 3) ||
+      q_nope_stride_token % 2 || q_nope_stride_head % 2 || q_pe_stride_token % 2 ||
+      q_pe_stride_head % 2)
+    return fail(DSA_ERR_INVALID_ARG, "q rows must be 4-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(output) & 7) || out_stride_token % 4 || out_stride_head % 4)
+    return fail(DSA_ERR_INVALID_ARG, "output rows must be 8-byte aligned");
+  const int nst = stages_choice();
+  Plan pl;
+  int rc = make_plan(num_tokens, num_heads, topk, nst, &pl);
+  if (rc) return rc;
+  if (workspace_bytes < pl.bytes || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return fail(DSA_ERR_WORKSPACE, "workspace too small or not 256-byte aligned");
+
+  AttnParams p;
+  p.q_nope = static_cast<const __nv_bfloat16*>(q_nope);
+  p.q_pe = static_cast<const __nv_bfloat16*>(q_pe);
+  p.ckv = static_cast<const __nv_bfloat16*>(ckv_cache);
+  p.kpe = static_cast<const __nv_bfloat16*>(kpe_cache);
+  p.idx = sparse_indices;
+  p.out = static_cast<__nv_bfloat16*>(output);
+  p.lse = lse;
+  p.qn_st = q_nope_stride_token;
+  p.qn_sh = q_nope_stride_head;
+  p.qp_st = q_pe_stride_token;
+  p.qp_sh = q_pe_stride_head;
+  p.ckv_sp = ckv_stride_page;
+  p.ckv_sr = ckv_stride_row;
+  p.kpe_sp = kpe_stride_page;
+  p.kpe_sr = kpe_stride_row;
+  p.idx_st = indices_stride_token;
+  p.out_st = out_stride_token;
+  p.out_sh = out_stride_head;
+  p.lse_st = lse_stride_token;
+  p.lse_sh = lse_stride_head;
+  p.num_slots = num_pages * 64;
+  p.head_groups = (int)(num_heads / kHeads);
+  p.tiles_per_token = (int)(topk / kRows);
+  p.scale_log2 = sm_scale * 1.4426950408889634f;
+  p.tiles_base = pl.base;
+  p.tiles_rem = pl.rem;
+  p.max_seg = pl.max_seg;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  p.err = reinterpret_cast<int*>(ws);
+  p.counters = reinterpret_cast<int*>(ws + 256);
+  p.part = reinterpret_cast<float*>(ws + pl.part_off);
+
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = nst == 2 ? launch<2>(p, pl.ctas, st)
+                           : nst == 3 ? launch<3>(p, pl.ctas, st) : launch<4>(p, pl.ctas, st);
+  if (e != cudaSuccess) return fail(DSA_ERR_CUDA, cudaGetErrorString(e));
+  return DSA_OK;
+}
+
+int dsa_read_device_error(const void* workspace, int clear, int* bits, void* stream) {
+  if (!workspace || !bits) return fail(DSA_ERR_INVALID_ARG, "NULL pointer argument");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int h = 0;
+  cudaError_t e = cudaMemcpyAsync(&h, workspace, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess && clear && h)
+    e = cudaMemsetAsync(const_cast<void*>(workspace), 0, sizeof(int), st);
+  if (e != cudaSuccess) return fail(DSA_ERR_CUDA, cudaGetErrorString(e));
+  *bits = h;
+  return DSA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,162 @@
+"""Drop-in `kernel` for the DSA sparse-attention operator.
+
+Same name, arguments, return values and shape checks as the reference entry
+point `kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale)
+-> (output, lse)` (solution/triton/kernel.py:138-182, entry point named in
+config.toml:8, destination_passing_style = false).  The work runs in the
+sm_100a CUDA kernel of libdsa_b200.so, called through its C ABI on torch's
+current stream.  There is no Triton, no dispatch and no CPU fallback: CPU
+tensors or a missing library raise.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from . import _lib
+
+NUM_HEADS = 16
+HEAD_DIM_CKV = 512
+HEAD_DIM_KPE = 64
+PAGE_SIZE = 64
+TOPK = 2048
+
+
+class _Workspace:
+    """Per-device persistent workspace (error word, per-token counters,
+    split-K partials).  Zero-filled when allocated; the kernel leaves its
+    counters at zero, and the counter region is re-zeroed on the stream when
+    a call needs more counters than any earlier call on this buffer."""
+
+    def __init__(self):
+        self.buf = None
+        self.max_vtokens = 0
+        self.lock = threading.Lock()
+
+    def get(self, device, nbytes, vtokens, stream):
+        with self.lock:
+            if self.buf is None or self.buf.numel() < nbytes:
+                self.buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+                self.max_vtokens = 0
+            if vtokens > self.max_vtokens:
+                self.buf[256: 256 + 4 * vtokens].zero_()
+                self.max_vtokens = vtokens
+            return self.buf
+
+
+_workspaces: dict[int, _Workspace] = {}
+
+
+def workspace_for(device: torch.device) -> _Workspace:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _workspaces.get(idx)
+    if ws is None:
+        ws = _workspaces.setdefault(idx, _Workspace())
+    return ws
+
+
+def _rowmajor(t: torch.Tensor, align_elems: int) -> torch.Tensor:
+    """Keep strided views when the last dim is contiguous and rows are aligned."""
+    ok = t.stride(-1) == 1 and all(s % align_elems == 0 for s in t.stride()[:-1])
+    ok = ok and (t.data_ptr() % (2 * align_elems) == 0)
+    return t if ok else t.contiguous()
+
+
+def _check_inputs(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices):
+    num_tokens, num_qo_heads, head_dim_ckv = q_nope.shape
+    num_pages, page_size, _ = ckv_cache.shape
+    head_dim_kpe = q_pe.shape[-1]
+    topk = sparse_indices.shape[-1]
+    # the reference's static assertions (kernel.py:147-151); heads may be any
+    # multiple of 16 here (independent 16-head groups sharing the indices)
+    assert num_qo_heads % NUM_HEADS == 0 and num_qo_heads > 0
+    assert head_dim_ckv == HEAD_DIM_CKV
+    assert head_dim_kpe == HEAD_DIM_KPE
+    assert page_size == PAGE_SIZE
+    assert topk % 32 == 0 and topk > 0
+    assert q_pe.shape[:2] == q_nope.shape[:2]
+    assert kpe_cache.shape == (num_pages, page_size, head_dim_kpe)
+    assert sparse_indices.shape[0] == num_tokens
+    for name, t in (("q_nope", q_nope), ("q_pe", q_pe), ("ckv_cache", ckv_cache),
+                    ("kpe_cache", kpe_cache), ("sparse_indices", sparse_indices)):
+        if not t.is_cuda:
+            raise RuntimeError(f"{name} must be a CUDA tensor (no CPU path)")
+    for name, t in (("q_nope", q_nope), ("q_pe", q_pe), ("ckv_cache", ckv_cache),
+                    ("kpe_cache", kpe_cache)):
+        assert t.dtype == torch.bfloat16, f"{name} must be bfloat16"
+    return num_tokens, num_qo_heads, num_pages, topk
+
+
+def kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, *, output=None,
+           lse=None):
+    """DSA sparse attention; returns (output [T,H,512] bf16, lse [T,H] fp32 base-2).
+
+    output/lse may be passed to write into existing tensors (same shapes);
+    by default they are allocated, like the reference (kernel.py:156-157).
+    """
+    num_tokens, heads, num_pages, topk = _check_inputs(q_nope, q_pe, ckv_cache, kpe_cache,
+                                                       sparse_indices)
+    device = q_nope.device
+    if output is None:
+        output = torch.empty((num_tokens, heads, HEAD_DIM_CKV), dtype=torch.bfloat16, device=device)
+    if lse is None:
+        lse = torch.empty((num_tokens, heads), dtype=torch.float32, device=device)
+    if num_tokens == 0:
+        return output, lse
+    if sparse_indices.dtype != torch.int32:
+        sparse_indices = sparse_indices.to(torch.int32)
+    if sparse_indices.stride(-1) != 1:
+        sparse_indices = sparse_indices.contiguous()
+    q_nope = _rowmajor(q_nope, 2)
+    q_pe = _rowmajor(q_pe, 2)
+    ckv_cache = _rowmajor(ckv_cache, 8)
+    kpe_cache = _rowmajor(kpe_cache, 8)
+    assert output.stride(-1) == 1 and lse.stride(-1) == 1
+
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device)
+        nbytes = ctypes.c_size_t(0)
+        _lib.call("dsa_sparse_attention_workspace_size", num_tokens, heads, topk,
+                  ctypes.byref(nbytes))
+        ws = workspace_for(device).get(device, nbytes.value, num_tokens * (heads // NUM_HEADS),
+                                       stream)
+        _lib.call(
+            "dsa_sparse_attention",
+            q_nope.data_ptr(), q_nope.stride(0), q_nope.stride(1),
+            q_pe.data_ptr(), q_pe.stride(0), q_pe.stride(1),
+            ckv_cache.data_ptr(), ckv_cache.stride(0), ckv_cache.stride(1),
+            kpe_cache.data_ptr(), kpe_cache.stride(0), kpe_cache.stride(1),
+            sparse_indices.data_ptr(), sparse_indices.stride(0),
+            num_tokens, heads, num_pages, PAGE_SIZE, topk, float(sm_scale),
+            output.data_ptr(), output.stride(0), output.stride(1),
+            lse.data_ptr(), lse.stride(0), lse.stride(1),
+            ws.data_ptr(), ws.numel(), ctypes.c_void_p(stream.cuda_stream))
+    return output, lse
+
+
+def kernel_splitk(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, SPLIT_K=None):
+    """Same signature as the reference's kernel_splitk (kernel.py:496).  The
+    split of the top-k dimension is chosen by occupancy inside the library,
+    so SPLIT_K is accepted for compatibility and ignored."""
+    return kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale)
+
+
+kernel_splitk_v2 = kernel_splitk
+
+
+def read_device_error(device=None, clear=True) -> int:
+    """Synchronise and return the DSA_DEVERR_* bits raised by kernels that
+    used this device's workspace (bad indices, timed-out waits)."""
+    device = torch.device(device) if device is not None else torch.device(
+        "cuda", torch.cuda.current_device())
+    ws = workspace_for(device).buf
+    if ws is None:
+        return 0
+    bits = ctypes.c_int(0)
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device)
+        _lib.call("dsa_read_device_error", ws.data_ptr(), int(clear), ctypes.byref(bits),
+                  ctypes.c_void_p(stream.cuda_stream))
+    return bits.value

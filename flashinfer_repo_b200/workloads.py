@@ -1,0 +1,194 @@
+"""Seeded synthetic workloads for the DSA decode path.
+
+The reference measures on the contest's real decode workloads, which are not
+available; these generators stand in for them with the shapes, sizes and
+value distributions of the five benchmark configurations:
+
+  cfg1  T=1, 16 heads, 64 pages (context 4096), shuffled page table
+  cfg2  T=64, per-request context ~U[1024, 65536], shuffled page tables,
+        2048 distinct positions per token (-1 padded when context < 2048)
+  cfg3  T=8, 128 heads, context 131072, top-k clustered (half in the last 4096)
+  cfg4  indexer: T=128, context 32768, FP8 keys + fp32 scales, FP8 queries
+  cfg5  chunked prefill: queries at positions 61440+i draw <= their position
+
+Host generators use numpy (PCG64) so that fixtures are reproducible on any
+machine; the device generators (torch, on the GPU) are used by the bench for
+the multi-GB caches, where only shapes and distributions matter.
+
+`sparse_indices` are flat physical slot ids page*64 + offset, -1 = padding,
+exactly the convention of the reference operator (solution/triton/kernel.py:74-75).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+
+H, DC, DP, PS, TOPK = 16, 512, 64, 64, 2048
+SM_SCALE = 1.0 / math.sqrt(192.0)
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even fp32 -> bf16, returned as uint16 bit patterns."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    r[nan] = ((u[nan] >> 16) | 0x40).astype(np.uint16)
+    return r
+
+
+def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return (np.ascontiguousarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_e4m3_bits(x: np.ndarray) -> np.ndarray:
+    """Saturating round-to-nearest-even fp32 -> OCP FP8 E4M3 (max 448), as uint8.
+
+    Built from the format definition: enumerate the 127 non-negative finite
+    codes and pick the nearest (ties to the even code)."""
+    codes = np.arange(0x7F, dtype=np.uint8)  # 0x00..0x7E (0x7F is NaN)
+    vals = e4m3_bits_to_f32(codes).astype(np.float64)
+    a = np.minimum(np.abs(np.asarray(x, dtype=np.float64)), 448.0)
+    pos = np.searchsorted(vals, a)  # vals is increasing
+    pos = np.clip(pos, 1, len(vals) - 1)
+    lo, hi = vals[pos - 1], vals[pos]
+    pick_hi = (hi - a < a - lo) | ((hi - a == a - lo) & ((pos % 2) == 0))
+    code = np.where(pick_hi, pos, pos - 1).astype(np.uint8)
+    sign = (np.asarray(x) < 0) & (code != 0)
+    return (code | (sign.astype(np.uint8) << 7)).astype(np.uint8)
+
+
+def e4m3_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    b = np.asarray(b, dtype=np.uint8).astype(np.int32)
+    s = b >> 7
+    e = (b >> 3) & 0xF
+    m = b & 7
+    v = np.where(e == 0, np.ldexp(m.astype(np.float64), -9),
+                 np.ldexp((8 + m).astype(np.float64), e - 10))
+    v = np.where((e == 0xF) & (m == 7), np.nan, v)
+    return np.where(s == 1, -v, v).astype(np.float32)
+
+
+@dataclass
+class AttentionCase:
+    """One call of the sparse-attention operator (bf16 tensors as uint16 bits)."""
+    q_nope: np.ndarray      # [T, Hq, 512] uint16
+    q_pe: np.ndarray        # [T, Hq, 64] uint16
+    ckv: np.ndarray         # [P, 64, 512] uint16
+    kpe: np.ndarray         # [P, 64, 64] uint16
+    idx: np.ndarray         # [T, topk] int32 flat slot ids, -1 = padding
+    sm_scale: float
+    ctx: np.ndarray         # [T] context length of each token's request
+
+    @property
+    def T(self):
+        return self.idx.shape[0]
+
+
+def _positions(rng, ctx, topk, clustered=False):
+    """topk distinct positions in [0, ctx) (all of them when ctx < topk, -1 tail)."""
+    out = np.full(topk, -1, np.int64)
+    if ctx <= topk:
+        out[:ctx] = rng.permutation(ctx)
+        return out
+    if clustered and ctx > 4096 + topk:
+        half = topk // 2
+        recent = ctx - 4096 + rng.choice(4096, half, replace=False)
+        rest = rng.choice(ctx - 4096, topk - half, replace=False)
+        out[:] = rng.permutation(np.concatenate([recent, rest]))
+        return out
+    out[:] = rng.choice(ctx, topk, replace=False)
+    return out
+
+
+def make_attention_case(seed: int, ctx_lens, heads: int = H, topk: int = TOPK,
+                        kv_std: float = 0.5, clustered: bool = False,
+                        sm_scale: float = SM_SCALE, shared_cache: bool = False) -> AttentionCase:
+    """Build a batch whose token t belongs to a request of context ctx_lens[t].
+
+    Each request owns ceil(ctx/64) pages drawn from one global permutation of
+    all pages (shuffled page tables).  With shared_cache=True all tokens share
+    one request's pages (cfg1 / cfg3 style).
+    """
+    rng = np.random.default_rng(seed)
+    ctx_lens = np.asarray(ctx_lens, dtype=np.int64)
+    T = len(ctx_lens)
+    npages_req = (ctx_lens + PS - 1) // PS
+    if shared_cache:
+        P = int(npages_req.max())
+        perm = rng.permutation(P)
+        tables = [perm[: npages_req[t]] for t in range(T)]
+    else:
+        P = int(npages_req.sum())
+        perm = rng.permutation(P)
+        off = np.concatenate([[0], np.cumsum(npages_req)])
+        tables = [perm[off[t]: off[t + 1]] for t in range(T)]
+    q_nope = f32_to_bf16_bits(rng.standard_normal((T, heads, DC), dtype=np.float32))
+    q_pe = f32_to_bf16_bits(rng.standard_normal((T, heads, DP), dtype=np.float32))
+    ckv = f32_to_bf16_bits(rng.standard_normal((P, PS, DC), dtype=np.float32) * kv_std)
+    kpe = f32_to_bf16_bits(rng.standard_normal((P, PS, DP), dtype=np.float32) * kv_std)
+    idx = np.full((T, topk), -1, np.int32)
+    for t in range(T):
+        pos = _positions(rng, int(ctx_lens[t]), topk, clustered)
+        v = pos >= 0
+        idx[t, v] = (tables[t][pos[v] // PS] * PS + pos[v] % PS).astype(np.int32)
+    return AttentionCase(q_nope, q_pe, ckv, kpe, idx, float(sm_scale), ctx_lens)
+
+
+def cfg1_case(seed: int = 0) -> AttentionCase:
+    """BASELINE cfg1: T=1, 64 pages (context 4096), page_table = randperm(64),
+    pos = 2048 distinct positions, idx = page_table[pos>>6]*64 + (pos&63)."""
+    return make_attention_case(seed, [4096], shared_cache=True)
+
+
+def cfg2_ctx_lens(seed: int, T: int = 64, lo: int = 1024, hi: int = 65536) -> np.ndarray:
+    rng = np.random.default_rng(seed + 7919)
+    return rng.integers(lo, hi + 1, size=T)
+
+
+# ---------------------------------------------------------------- indexer cfg4
+@dataclass
+class IndexerCase:
+    q: np.ndarray           # [B, 64, 128] uint8 e4m3
+    k: np.ndarray           # [P, 64, 128] uint8 e4m3
+    scale: np.ndarray       # [P, 64] float32
+    w: np.ndarray           # [B, 64] float32
+    block_table: np.ndarray # [B, maxP] int32
+    seq_lens: np.ndarray    # [B] int32
+
+
+def make_indexer_case(seed: int, seq_lens, heads: int = 64, exact: bool = False,
+                      tie_heavy: bool = False) -> IndexerCase:
+    """cfg4-style indexer inputs.  exact=True builds "exact by construction"
+    inputs (small-integer e4m3 values, power-of-two scales, weights with few
+    mantissa bits) so every score is exact in fp32 in any summation order;
+    tie_heavy=True additionally repeats key rows so that many scores tie."""
+    rng = np.random.default_rng(seed)
+    seq_lens = np.asarray(seq_lens, dtype=np.int32)
+    B = len(seq_lens)
+    npg = (seq_lens.astype(np.int64) + PS - 1) // PS
+    P = int(npg.sum())
+    perm = rng.permutation(P).astype(np.int32)
+    maxp = int(npg.max())
+    bt = np.zeros((B, maxp), np.int32)
+    off = 0
+    for b in range(B):
+        bt[b, : npg[b]] = perm[off: off + npg[b]]
+        off += npg[b]
+    if exact:
+        q = f32_to_e4m3_bits(rng.integers(-3, 4, (B, heads, 128)).astype(np.float32))
+        kv = rng.integers(-3, 4, (P, PS, 128)).astype(np.float32)
+        if tie_heavy:
+            kv = kv[:, :, :]
+            kv[:, 1::2] = kv[:, 0::2]
+            kv[:, :, 8:] = 0
+        k = f32_to_e4m3_bits(kv)
+        scale = np.ldexp(1.0, rng.integers(-1, 2, (P, PS))).astype(np.float32)
+        w = (rng.integers(-8, 9, (B, heads)) / 16.0).astype(np.float32)
+    else:
+        q = f32_to_e4m3_bits(rng.standard_normal((B, heads, 128)))
+        k = f32_to_e4m3_bits(rng.standard_normal((P, PS, 128)))
+        scale = rng.uniform(0.5, 2.0, (P, PS)).astype(np.float32)
+        w = (rng.standard_normal((B, heads)) / 8.0).astype(np.float32)
+    return IndexerCase(q, k, scale, w, bt, seq_lens)

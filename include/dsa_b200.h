@@ -1,0 +1,103 @@
+/*
+ * dsa_b200.h -- C ABI of the B200 (sm_100a) DeepSeek-sparse-attention library.
+ *
+ * Plain pointers, sizes and element strides; no framework types.  Every call
+ * is asynchronous on the given CUDA stream (a cudaStream_t passed as void*,
+ * NULL = legacy default stream) and returns a dsa_status code; the message of
+ * the last failing call on the calling host thread is available from
+ * dsa_last_error_message().  Device pointers must be on the current device.
+ *
+ * Reference interfaces replaced (Starkdoorstep12/flashinfer-repo):
+ *   dsa_sparse_attention      <- solution/triton/kernel.py:138-182 `kernel`
+ *                                (and the split-K variants kernel.py:496-567,
+ *                                707-799, which compute the same function);
+ *                                the CUDA/TVM-FFI slot the reference leaves
+ *                                empty is solution/cuda/binding.py:14-25 and
+ *                                solution/cuda/kernel.cu:13-20.
+ *   dsa_indexer_scores        <- solution/triton/indexer_kernel.py:4-287
+ *                                `indexer_kernel` (+ launch at :386-409)
+ *   dsa_topk_select           <- solution/triton/indexer_kernel.py:289-343
+ *                                `topk_kernel` (+ launch at :422-431)
+ *   dsa_indexer_topk          <- solution/triton/indexer_kernel.py:345-433
+ *                                `run_indexer_and_topk`
+ */
+#ifndef DSA_B200_H_
+#define DSA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes returned by every entry point. */
+enum dsa_status {
+  DSA_OK = 0,
+  DSA_ERR_INVALID_ARG = 1, /* NULL pointer, negative size, misaligned row */
+  DSA_ERR_UNSUPPORTED = 2, /* shape outside what the kernels implement */
+  DSA_ERR_WORKSPACE = 3,   /* workspace too small or misaligned */
+  DSA_ERR_CUDA = 4         /* a CUDA runtime call failed (message has details) */
+};
+
+/* Bits of the device error word (first int of a workspace). */
+enum dsa_device_error {
+  DSA_DEVERR_BAD_INDEX = 1, /* an index outside [-1, num_pages*64): row skipped */
+  DSA_DEVERR_TIMEOUT = 2    /* a bounded wait inside a kernel gave up */
+};
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char* dsa_last_error_message(void);
+
+/*
+ * Workspace bytes dsa_sparse_attention needs for this shape on the current
+ * device.  The workspace holds a device error word, one arrival counter per
+ * (token, 16-head group) and the split-K partial results.
+ */
+int dsa_sparse_attention_workspace_size(int64_t num_tokens, int64_t num_heads, int64_t topk,
+                                        size_t* bytes);
+
+/*
+ * Sparse MLA attention over a paged latent cache (one decode step).
+ * Replaces kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale)
+ * -> (output, lse) of solution/triton/kernel.py:138-182.
+ *
+ *   q_nope  [T, H, 512] bf16     q_pe [T, H, 64] bf16        (H = 16*k)
+ *   ckv     [num_pages, 64, 512] bf16, kpe [num_pages, 64, 64] bf16
+ *   sparse_indices [T, topk] int32: flat slot ids page*64+offset, -1 = pad
+ *   output  [T, H, 512] bf16     lse [T, H] fp32 (base-2 log-sum-exp)
+ * Strides are in elements; the last dimension of every tensor is contiguous.
+ * Cache rows must be 16-byte aligned, q rows 4-byte, output rows 8-byte.
+ * A token with no valid index gets output 0 and lse -inf (kernel.py:118-136).
+ * page_size must be 64 and topk a multiple of 32 (the reference asserts
+ * H=16, page_size=64, topk=2048, kernel.py:147-151; H>16 is handled as
+ * independent 16-head groups sharing the same indices).
+ *
+ * workspace: >= dsa_sparse_attention_workspace_size() bytes, 256-byte aligned,
+ * ZERO-FILLED before its first use (and again if it is reused for a larger
+ * num_tokens*num_heads).  Every call leaves its counters at zero, so the same
+ * workspace can be reused by later calls on the same stream.  Calls that
+ * share one workspace must not overlap in time.
+ */
+int dsa_sparse_attention(const void* q_nope, int64_t q_nope_stride_token, int64_t q_nope_stride_head,
+                         const void* q_pe, int64_t q_pe_stride_token, int64_t q_pe_stride_head,
+                         const void* ckv_cache, int64_t ckv_stride_page, int64_t ckv_stride_row,
+                         const void* kpe_cache, int64_t kpe_stride_page, int64_t kpe_stride_row,
+                         const int32_t* sparse_indices, int64_t indices_stride_token,
+                         int64_t num_tokens, int64_t num_heads, int64_t num_pages, int64_t page_size,
+                         int64_t topk, float sm_scale, void* output, int64_t out_stride_token,
+                         int64_t out_stride_head, float* lse, int64_t lse_stride_token,
+                         int64_t lse_stride_head, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+/*
+ * Read (and optionally clear) the device error word of a workspace.
+ * Synchronises the stream.  *bits receives DSA_DEVERR_* flags.
+ */
+int dsa_read_device_error(const void* workspace, int clear, int* bits, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSA_B200_H_ */
