@@ -61,7 +61,7 @@ struct AttnParams {
   int head_groups;      // heads / 16; virtual token v = t * head_groups + group
   int tiles_per_token;  // topk / 32
   float scale_log2;     // sm_scale * log2(e)
-  int tiles_base, tiles_rem, max_seg;
+  int tiles_base, tiles_rem;
   float* part;
   int* counters;
   int* err;
@@ -85,9 +85,11 @@ __device__ __forceinline__ int cta_of_tile(const AttnParams& p, int tile) {
   const int big = (p.tiles_base + 1) * p.tiles_rem;
   return tile < big ? tile / (p.tiles_base + 1) : p.tiles_rem + (tile - big) / p.tiles_base;
 }
+// Only a CTA's first and last token segments can be partial (every token
+// strictly inside its range is complete), so two partial slots per CTA.
 __device__ __forceinline__ float* part_slot(const AttnParams& p, int c, int v) {
-  const int j = v - cta_start(p, c) / p.tiles_per_token;
-  return p.part + (int64_t)(c * p.max_seg + j) * kPartFloats;
+  const int j = (v == cta_start(p, c) / p.tiles_per_token) ? 0 : 1;
+  return p.part + (int64_t)(2 * c + j) * kPartFloats;
 }
 
 // ------------------------------------------------------------------ producer
@@ -504,7 +506,7 @@ int device_slots(int nst, int* sms_out) {
 }
 
 struct Plan {
-  int ctas, base, rem, max_seg;
+  int ctas, base, rem;
   int64_t vtokens, total_tiles;
   size_t part_off, bytes;
 };
@@ -528,10 +530,8 @@ int make_plan(int64_t num_tokens, int64_t heads, int64_t topk, int nst, Plan* pl
   pl->ctas = (int)ctas;
   pl->base = (int)(pl->total_tiles / ctas);
   pl->rem = (int)(pl->total_tiles % ctas);
-  const int64_t longest = pl->base + (pl->rem ? 1 : 0);
-  pl->max_seg = (int)((longest + tpt - 2) / tpt + 1);
   pl->part_off = align256(256 + 4 * (size_t)pl->vtokens);
-  pl->bytes = pl->part_off + (size_t)pl->ctas * pl->max_seg * kPartFloats * sizeof(float);
+  pl->bytes = pl->part_off + (size_t)pl->ctas * 2 * kPartFloats * sizeof(float);
   return DSA_OK;
 }
 
@@ -546,6 +546,8 @@ cudaError_t launch(const AttnParams& p, int ctas, cudaStream_t st) {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace
+
+int report_error(int code, const char* msg) { return fail(code, msg); }
 
 }  // namespace dsa
 
@@ -633,7 +635,6 @@ int dsa_sparse_attention(const void* q_nope, int64_t q_nope_stride_token, int64_
   p.scale_log2 = sm_scale * 1.4426950408889634f;
   p.tiles_base = pl.base;
   p.tiles_rem = pl.rem;
-  p.max_seg = pl.max_seg;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   p.err = reinterpret_cast<int*>(ws);
   p.counters = reinterpret_cast<int*>(ws + 256);

@@ -123,6 +123,9 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Host side: record `msg` as this thread's dsa_last_error_message() and return code.
+int report_error(int code, const char* msg);
+
 __device__ __forceinline__ void set_error(int* err, int bits) {
   if (err) atomicOr(err, bits);
 }
