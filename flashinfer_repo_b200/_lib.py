@@ -23,6 +23,8 @@ SIGNATURES = {
     "dsa_sparse_attention_workspace_size": [I64, I64, I64, ctypes.POINTER(SZ)],
     "dsa_sparse_attention": [P, I64, I64, P, I64, I64, P, I64, I64, P, I64, I64, P, I64,
                              I64, I64, I64, I64, I64, F32, P, I64, I64, P, I64, I64, P, SZ, P],
+    "dsa_sparse_attention_noalloc": [P, I64, I64, P, I64, I64, P, I64, I64, P, I64, I64, P, I64,
+                                     I64, I64, I64, I64, I64, F32, P, I64, I64, P, I64, I64, P],
     "dsa_read_device_error": [P, INT, ctypes.POINTER(INT), P],
 }
 

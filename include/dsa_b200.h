@@ -91,6 +91,34 @@ int dsa_sparse_attention(const void* q_nope, int64_t q_nope_stride_token, int64_
                          void* stream);
 
 /*
+ * dsa_sparse_attention_noalloc -- the same operation, arguments and results as
+ * dsa_sparse_attention, without the workspace arguments.  This entry point has
+ * no counterpart in the reference.  It exists for callers that cannot
+ * allocate device memory when they call the operator: engines that reserve
+ * nearly all free HBM for the KV cache at start-up and pass every later
+ * allocation through their own pool, and plugin hosts that hand an operator
+ * only its inputs and outputs, with no workspace and no allocator.  The
+ * scratch lives in a static device array of the library (about 20 MiB on
+ * every device that loads it, held until the process exits).  Limits:
+ * num_tokens*num_heads/16 <= 8192 and a grid of at most 320 CTAs; larger calls
+ * return DSA_ERR_UNSUPPORTED without launching.  The first call on a device
+ * looks up the array's address (do it before any stream capture).  All calls
+ * on a device share the array: calls that overlap on the GPU race and must be
+ * serialised by the caller.  No cudaMalloc/cudaFree is called.
+ */
+int dsa_sparse_attention_noalloc(const void* q_nope, int64_t q_nope_stride_token,
+                                 int64_t q_nope_stride_head, const void* q_pe,
+                                 int64_t q_pe_stride_token, int64_t q_pe_stride_head,
+                                 const void* ckv_cache, int64_t ckv_stride_page,
+                                 int64_t ckv_stride_row, const void* kpe_cache,
+                                 int64_t kpe_stride_page, int64_t kpe_stride_row,
+                                 const int32_t* sparse_indices, int64_t indices_stride_token,
+                                 int64_t num_tokens, int64_t num_heads, int64_t num_pages,
+                                 int64_t page_size, int64_t topk, float sm_scale, void* output,
+                                 int64_t out_stride_token, int64_t out_stride_head, float* lse,
+                                 int64_t lse_stride_token, int64_t lse_stride_head, void* stream);
+
+/*
  * Read (and optionally clear) the device error word of a workspace.
  * Synchronises the stream.  *bits receives DSA_DEVERR_* flags.
  */
