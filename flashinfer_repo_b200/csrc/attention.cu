@@ -71,7 +71,7 @@ template <int NST>
 struct AttnSmem {
   uint8_t ckv[NST][kRows * kCkvStride];
   uint8_t kpe[NST][kRows * kKpeStride];
-  float4 sred[2][kCWarps][32][4];
+  float4 sred[2][kCWarps][4][32];  // [buf][warp][n-block][lane]: conflict-free
   uint32_t vmask[NST];
   uint64_t full[NST];
   uint64_t empty[NST];
@@ -96,18 +96,31 @@ __device__ __forceinline__ float* part_slot(const AttnParams& p, int c, int v) {
 template <int NST>
 __device__ __forceinline__ void attn_producer(const AttnParams& p, AttnSmem<NST>& S, int lane,
                                               int tile_begin, int tile_end) {
+  // Indices are fetched kIdxAhead tiles before use so that the dependent
+  // global load is off the critical path of the row copies.
+  constexpr int kIdxAhead = 3;
+  auto load_idx = [&](int tile) -> int32_t {
+    if (tile >= tile_end) return -1;
+    const int v = tile / p.tiles_per_token;
+    const int t = v / p.head_groups;
+    const int r0 = (tile - v * p.tiles_per_token) * kRows;
+    return __ldg(p.idx + (int64_t)t * p.idx_st + r0 + lane);
+  };
+  int32_t ring[kIdxAhead];
+#pragma unroll
+  for (int k = 0; k < kIdxAhead; ++k) ring[k] = load_idx(tile_begin + k);
   int it = 0;
   for (int tile = tile_begin; tile < tile_end; ++tile, ++it) {
     const int s = it % NST;
     const uint32_t ph = (it / NST) & 1;
+    const int32_t id = ring[0];
+#pragma unroll
+    for (int k = 0; k + 1 < kIdxAhead; ++k) ring[k] = ring[k + 1];
+    ring[kIdxAhead - 1] = load_idx(tile + kIdxAhead);
     if (!mbar_wait(&S.empty[s], ph ^ 1)) {
       set_error(p.err, kErrTimeout);
       break;
     }
-    const int v = tile / p.tiles_per_token;
-    const int t = v / p.head_groups;
-    const int r0 = (tile - v * p.tiles_per_token) * kRows;
-    const int32_t id = __ldg(p.idx + (int64_t)t * p.idx_st + r0 + lane);
     const bool valid = id >= 0 && id < p.num_slots;
     if (id < -1 || id >= p.num_slots) set_error(p.err, kErrBadIndex);
     const uint32_t mask = __ballot_sync(0xffffffffu, valid);
@@ -286,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, (NST == 2 ? 2 : 1)) dsa_attention_ke
       }
 #pragma unroll
       for (int nb = 0; nb < 4; ++nb)
-        S.sred[buf][warp][lane][nb] = make_float4(sc[nb][0], sc[nb][1], sc[nb][2], sc[nb][3]);
+        S.sred[buf][warp][nb][lane] = make_float4(sc[nb][0], sc[nb][1], sc[nb][2], sc[nb][3]);
       named_bar_sync(1, kCWarps * 32);
       float x[4][4];
 #pragma unroll
@@ -295,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, (NST == 2 ? 2 : 1)) dsa_attention_ke
       for (int w = 0; w < kCWarps; ++w) {
 #pragma unroll
         for (int nb = 0; nb < 4; ++nb) {
-          const float4 a = S.sred[buf][w][lane][nb];
+          const float4 a = S.sred[buf][w][nb][lane];
           x[nb][0] += a.x;
           x[nb][1] += a.y;
           x[nb][2] += a.z;
