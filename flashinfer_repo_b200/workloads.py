@@ -159,7 +159,7 @@ class IndexerCase:
 
 
 def make_indexer_case(seed: int, seq_lens, heads: int = 64, exact: bool = False,
-                      tie_heavy: bool = False) -> IndexerCase:
+                      tie_heavy: bool = False, fast: bool = False) -> IndexerCase:
     """cfg4-style indexer inputs.  exact=True builds "exact by construction"
     inputs (small-integer e4m3 values, power-of-two scales, weights with few
     mantissa bits) so every score is exact in fp32 in any summation order;
@@ -186,6 +186,13 @@ def make_indexer_case(seed: int, seq_lens, heads: int = 64, exact: bool = False,
         k = f32_to_e4m3_bits(kv)
         scale = np.ldexp(1.0, rng.integers(-1, 2, (P, PS))).astype(np.float32)
         w = (rng.integers(-8, 9, (B, heads)) / 16.0).astype(np.float32)
+    elif fast:
+        # large cases: uniformly random finite e4m3 codes (no fp32 round trip)
+        q = f32_to_e4m3_bits(rng.standard_normal((B, heads, 128)))
+        k = rng.integers(0, 256, (P, PS, 128), dtype=np.uint8)
+        k[(k & 0x7F) == 0x7F] ^= 1
+        scale = rng.uniform(0.5, 2.0, (P, PS)).astype(np.float32)
+        w = (rng.standard_normal((B, heads)) / 8.0).astype(np.float32)
     else:
         q = f32_to_e4m3_bits(rng.standard_normal((B, heads, 128)))
         k = f32_to_e4m3_bits(rng.standard_normal((P, PS, 128)))

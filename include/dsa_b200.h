@@ -119,6 +119,54 @@ int dsa_sparse_attention_noalloc(const void* q_nope, int64_t q_nope_stride_token
                                  int64_t lse_stride_token, int64_t lse_stride_head, void* stream);
 
 /*
+ * FP8 lightning-indexer scores.  Replaces indexer_kernel
+ * (solution/triton/indexer_kernel.py:4-287, launched at :386-409):
+ *   scores[b*scores_stride + t] = scale(t) * sum_h w[b,h] * ReLU(q[b,h,:] . k8(t))
+ * for every token position t < seq_lens[b] (other entries are not written).
+ *   q_fp8        [batch, 64, 128] e4m3, contiguous, 16-byte aligned
+ *   k_cache_fp8  key row of (page, slot) at k_cache_fp8 + page*k_page_stride
+ *                + slot*128 bytes (e4m3), 64 slots per page
+ *   k_scale      fp32 scale of (page, slot) at k_scale + page*scale_page_stride
+ *                + slot*4 bytes (split [P,64] tensor or page-packed layout)
+ *   weights      [batch, 64] fp32; block_table [batch, *] int32 logical page ->
+ *                physical page; seq_lens [batch] int32 (device pointers)
+ * num_heads must be 64 and head_dim 128.  max_len bounds every seq_len (e.g.
+ * block-table width * 64).  device_error (may be NULL) receives DSA_DEVERR_*
+ * bits (a page id outside [0, num_pages) is flagged and its rows skipped).
+ */
+int dsa_indexer_scores(const void* q_fp8, const void* k_cache_fp8, int64_t k_page_stride,
+                       const void* k_scale, int64_t scale_page_stride, const float* weights,
+                       const int32_t* block_table, int64_t block_table_stride,
+                       const int32_t* seq_lens, int64_t batch, int64_t num_heads, int64_t head_dim,
+                       int64_t num_pages, int64_t max_len, float* scores, int64_t scores_stride,
+                       int* device_error, void* stream);
+
+/*
+ * Exact top-k of each request's scores.  Replaces topk_kernel
+ * (solution/triton/indexer_kernel.py:289-343, launched at :422-431): the
+ * min(k, seq_lens[b]) positions with the largest scores, in descending score,
+ * ties toward the lower position, then -1.  positions[b, j] is the token
+ * position inside the request; slots[b, j] (optional, NULL to skip) is the
+ * flat physical slot block_table[b, pos/64]*64 + pos%64 that
+ * dsa_sparse_attention consumes.  1 <= k <= 2048.
+ */
+int dsa_topk_select(const float* scores, int64_t scores_stride, const int32_t* seq_lens,
+                    const int32_t* block_table, int64_t block_table_stride, int64_t batch, int64_t k,
+                    int32_t* positions, int32_t* slots, void* stream);
+
+/*
+ * Indexer scores followed by top-k (replaces run_indexer_and_topk,
+ * solution/triton/indexer_kernel.py:345-433, without its two device-to-host
+ * synchronisations).  scores_workspace holds batch*max_len floats.
+ */
+int dsa_indexer_topk(const void* q_fp8, const void* k_cache_fp8, int64_t k_page_stride,
+                     const void* k_scale, int64_t scale_page_stride, const float* weights,
+                     const int32_t* block_table, int64_t block_table_stride, const int32_t* seq_lens,
+                     int64_t batch, int64_t num_heads, int64_t head_dim, int64_t num_pages,
+                     int64_t max_len, int64_t k, float* scores_workspace, int32_t* positions,
+                     int32_t* slots, int* device_error, void* stream);
+
+/*
  * Read (and optionally clear) the device error word of a workspace.
  * Synchronises the stream.  *bits receives DSA_DEVERR_* flags.
  */

@@ -47,3 +47,18 @@ def assert_attention_close(out, lse, ref_out_bits, ref_lse, what=""):
         err = np.abs(got_lse[~inf_ref] - ref_lse[~inf_ref]).max()
         assert err <= LSE_ATOL, f"{what}: LSE max abs err {err:.3g}"
     return float(abs_err.max())
+
+
+def indexer_case_to_device(case, device):
+    """IndexerCase -> (q fp8, k fp8, scale, w, seq_lens, block_table) on `device`."""
+    f8 = torch.float8_e4m3fn
+    return (torch.from_numpy(case.q).to(device).view(f8), torch.from_numpy(case.k).to(device).view(f8),
+            torch.from_numpy(case.scale).to(device), torch.from_numpy(case.w).to(device),
+            torch.from_numpy(case.seq_lens).to(device), torch.from_numpy(case.block_table).to(device))
+
+
+def oracle_indexer(case, max_len):
+    from oracle import oracle as O
+    P = case.k.shape[0]
+    return O.indexer_scores(case.q, case.k.reshape(P, -1), 64 * 128, case.scale.reshape(P, -1), 64 * 4,
+                            case.w, case.block_table, case.seq_lens, max_len)
