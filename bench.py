@@ -292,6 +292,63 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_cfg4(args):
+    """BASELINE cfg4: one DSA decode step = FP8 indexer over 128 requests x
+    32768 tokens -> exact top-2048 -> 16-head sparse MLA attention on the
+    selected slots.  Reports per-kernel device time and the indexer roofline."""
+    rank, world, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from flashinfer_repo_b200 import indexer as IX
+    from flashinfer_repo_b200 import kernel
+    from flashinfer_repo_b200.bench_inputs import attention_bytes, indexer_bytes, make_cfg4_device
+    d = make_cfg4_device(seed=2000 + rank, device=dev, T=args.requests)
+    T = d["seq_lens"].numel()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    scores = torch.empty((T, d["block_table"].shape[1] * 64), dtype=torch.float32, device=dev)
+
+    def step(ev=None):
+        if ev: ev[0].record(stream)
+        IX.indexer_scores(d["q8"], d["k8"], d["scale"], d["w"], d["seq_lens"], d["block_table"], out=scores)
+        if ev: ev[1].record(stream)
+        pos, slots = IX.topk_select(scores, d["seq_lens"], d["block_table"], 2048)
+        if ev: ev[2].record(stream)
+        out, lse = kernel(d["q_nope"], d["q_pe"], d["ckv"], d["kpe"], slots, d["sm_scale"])
+        if ev: ev[3].record(stream)
+        return slots
+    for _ in range(args.warmup):
+        flush.fill_(1)
+        step()
+    torch.cuda.synchronize()
+    parts = np.zeros(3)
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            slots = step(ev)
+            ev[3].synchronize()
+            parts += [ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]), ev[2].elapsed_time(ev[3])]
+    parts /= args.steps
+    total = parts.sum()
+    ib = indexer_bytes(d["seq_lens"])
+    peak, kind = peaks()
+    print(json.dumps({
+        "metric": "DSA decode step (indexer + top-k + attention) query-tokens/sec", "value": T / (total / 1e3),
+        "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": total,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp8+bf16",
+        "data": "synthetic (seeded, BASELINE cfg4 shapes and distributions)",
+        "config": {"workload": "cfg4: T=128 requests, ctx 32768, FP8 indexer 64x128, top-2048, 16-head MLA",
+                   "l2": "flushed before every step (256 MiB write, untimed)"},
+        "kernels_ms": {"indexer": parts[0], "topk": parts[1], "attention": parts[2]},
+        "roofline": {"bound": "hbm", "kernel": "dsa_indexer_kernel", "achieved": ib / (parts[0] / 1e3) / 1e9,
+                     "peak": peak, "unit": "GB/s", "frac": ib / (parts[0] / 1e3) / 1e9 / peak,
+                     "traffic": None, "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({kind})"},
+        "attention_roofline": {"achieved": attention_bytes(slots) / (parts[2] / 1e3) / 1e9, "unit": "GB/s"},
+        "gpu_launches": 3 * args.steps, "clocks": clk.summary(),
+    }), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -299,11 +356,16 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg4"],
+                    help="cfg2 = headline batched decode; cfg4 = indexer + top-k + attention")
+    ap.add_argument("--requests", type=int, default=128, help="cfg4 requests per GPU (default 128)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference_arm(args)
+    elif args.workload == "cfg4":
+        run_cfg4(args)
     else:
         run_ours(args)
 

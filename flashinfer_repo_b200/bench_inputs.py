@@ -93,3 +93,35 @@ def attention_flops(idx: torch.Tensor, heads: int = 16) -> int:
     n_valid = int((idx >= 0).sum().item())
     return 2 * heads * n_valid * (DC + DP) + 2 * heads * n_valid * DC
 
+
+
+def make_cfg4_device(seed=0, device="cuda", T=128, ctx=32768, heads=16):
+    """BASELINE cfg4: T=128 requests of context 32768; index keys e4m3
+    [P,64,128] (uniform finite codes), fp32 scales U(0.5,2), index queries e4m3
+    [T,64,128] from N(0,1), head weights N(0,1)/8; the latent cache for the
+    16-head attention over the same pages.  Returns a dict of tensors."""
+    g = _gen(seed, device)
+    npg = (ctx + PS - 1) // PS
+    P = T * npg
+    perm = torch.randperm(P, generator=g, device=device).to(torch.int32)
+    block_table = perm.view(T, npg).contiguous()
+    k8 = torch.randint(0, 256, (P, PS, 128), generator=g, device=device, dtype=torch.int32).to(torch.uint8)
+    k8 = torch.where((k8 & 0x7F) == 0x7F, k8 ^ 1, k8)
+    scale = torch.rand((P, PS), generator=g, device=device) * 1.5 + 0.5
+    q8 = torch.randn((T, 64, 128), generator=g, device=device).clamp(-448, 448).to(torch.float8_e4m3fn)
+    w = torch.randn((T, 64), generator=g, device=device) / 8
+    seq_lens = torch.full((T,), ctx, dtype=torch.int32, device=device)
+    ckv = _randn_bf16((P, PS, DC), g, device, 0.5)
+    kpe = _randn_bf16((P, PS, DP), g, device, 0.5)
+    q_nope = _randn_bf16((T, heads, DC), g, device)
+    q_pe = _randn_bf16((T, heads, DP), g, device)
+    return dict(q8=q8, k8=k8, scale=scale, w=w, seq_lens=seq_lens, block_table=block_table,
+                ckv=ckv, kpe=kpe, q_nope=q_nope, q_pe=q_pe, sm_scale=SM_SCALE)
+
+
+def indexer_bytes(seq_lens, heads=64, topk=TOPK) -> int:
+    """Algorithmic HBM bytes of the indexer per call: per request
+    ctx*(128+4) keys+scales, 64*128 q, 64*4 weights, plus topk*4*2 outputs."""
+    ctx = int(seq_lens.sum().item())
+    B = seq_lens.numel()
+    return ctx * 132 + B * (heads * 128 + heads * 4 + topk * 8)

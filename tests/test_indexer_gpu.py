@@ -94,3 +94,20 @@ def test_full_size_cfg4(cuda_device):
     ref = oracle_indexer(sub, max_len)
     scale = np.abs(ref).max(axis=1, keepdims=True)
     assert (np.abs(scores[pick] - ref) <= 1e-5 * scale).all()
+
+
+@pytest.mark.parametrize("L", [40960, 40961, 65536, 2049])
+def test_topk_long_and_tied_rows(cuda_device, L):
+    """Rows longer than the shared-memory cache take the streaming path; heavy
+    ties (values on a coarse grid) exercise the lower-position rule."""
+    rng = np.random.default_rng(L)
+    B = 3
+    scores = np.round(rng.standard_normal((B, L)) * 4).astype(np.float32) / 4
+    scores[1] = 1.0  # every score equal
+    lens = np.array([L, L, L // 2], np.int32)
+    bt = rng.permutation(B * ((L + 63) // 64)).astype(np.int32).reshape(B, -1)
+    pos, slots = IX.topk_select(torch.from_numpy(scores).to(cuda_device), torch.from_numpy(lens).to(cuda_device),
+                                torch.from_numpy(bt).to(cuda_device), 2048)
+    rpos, rslots = O.topk(scores, lens, bt, 2048)
+    assert np.array_equal(pos.cpu().numpy(), rpos) and np.array_equal(slots.cpu().numpy(), rslots)
+    assert rpos[1].tolist() == list(range(2048))
