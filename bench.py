@@ -349,6 +349,79 @@ def run_cfg4(args):
     }), flush=True)
 
 
+def run_cfg3(args):
+    """BASELINE cfg3: T=8 tokens, 128 heads, context 131072, clustered top-k,
+    latent cache replicated on every GPU; heads sharded 128/N per rank and the
+    outputs all-gathered (NCCL).  Strong scaling: the job is fixed."""
+    rank, world, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import torch.distributed as dist
+    from flashinfer_repo_b200 import kernel
+    from flashinfer_repo_b200.bench_inputs import attention_bytes, make_cfg3_device
+    from flashinfer_repo_b200.parallel import head_sharded_attention
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    qn, qp, ckv, kpe, idx, scale = make_cfg3_device(seed=3000, device=dev)  # same on every rank
+    T, H = qn.shape[:2]
+    h = H // world
+    sl = slice(h * rank, h * (rank + 1))
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def step():
+        if world > 1:
+            return head_sharded_attention(qn, qp, ckv, kpe, idx, scale)
+        return kernel(qn, qp, ckv, kpe, idx, scale)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    k_ms, s_ms = [], []
+    for i in range(args.steps):
+        flush.fill_(i & 0xFF)
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        e[0].record(stream)
+        kernel(qn[:, sl], qp[:, sl], ckv, kpe, idx, scale)
+        e[1].record(stream)
+        flush.fill_(i & 0xFF)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        torch.cuda._sleep(200_000)  # keeps the GPU busy while the host enqueues the step
+        e[2].record(stream)
+        step()
+        e3 = torch.cuda.Event(enable_timing=True)
+        e3.record(stream)
+        e3.synchronize()
+        k_ms.append(e[0].elapsed_time(e[1]))
+        s_ms.append(e[2].elapsed_time(e3))
+    t = torch.tensor([statistics.median(k_ms), statistics.median(s_ms)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    kms, sms = t.tolist()
+    peak, kind = peaks()
+    if rank == 0:
+        ab = attention_bytes(idx) * (h // 16)  # the 16-head operator's bytes per head group
+        print(json.dumps({
+            "metric": "DSA decode query-tokens/sec, 128 heads (head-sharded)", "value": T / (sms / 1e3),
+            "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": sms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded, BASELINE cfg3 shapes and distributions)",
+            "config": {"workload": "cfg3: T=8, 128 heads, ctx 131072, clustered top-2048",
+                       "parallelism": f"heads {h}/rank x {world} + all-gather",
+                       "l2": "flushed before every step (256 MiB write, untimed)"},
+            "kernel_ms": kms, "step_ms_incl_allgather": sms,
+            "roofline": {"bound": "hbm", "kernel": "dsa_attention_kernel",
+                         "achieved": ab / (kms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": ab / (kms / 1e3) / 1e9 / peak, "traffic": None,
+                         "note": "algorithmic bytes per rank = 16-head operator bytes x head groups "
+                                 "(repeat row reads of the groups are served from L2)"},
+            "gpu_launches": args.steps * 2,
+        }), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -356,7 +429,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg4"],
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg3", "cfg4"],
                     help="cfg2 = headline batched decode; cfg4 = indexer + top-k + attention")
     ap.add_argument("--requests", type=int, default=128, help="cfg4 requests per GPU (default 128)")
     args = ap.parse_args()
@@ -366,6 +439,8 @@ def main():
         run_reference_arm(args)
     elif args.workload == "cfg4":
         run_cfg4(args)
+    elif args.workload == "cfg3":
+        run_cfg3(args)
     else:
         run_ours(args)
 
