@@ -23,9 +23,9 @@
 //    registers), partial scores reduced through shared memory; online
 //    softmax in registers (base-2, exp2); PV with each warp owning 128 of
 //    the 512 output columns; P is re-used from registers as the A operand.
-//  * A token split across CTAs writes unnormalised (acc, m, l) partials; the
-//    CTA that arrives last on the token's counter merges them (LSE merge of
-//    kernel.py:437-493) in the same launch.  Counters return to zero.
+//  * A token split across CTAs writes unnormalised (acc, m, l) partials; a
+//    second grid (one CTA per token and head, programmatic dependent launch)
+//    merges them (LSE merge of kernel.py:437-493) using every SM.
 #include <cstdio>
 #include <cstdlib>
 #include <mutex>
@@ -42,7 +42,8 @@ constexpr int kRows = 32;             // rows per tile
 constexpr int kCkvStride = 1040;      // smem pitch of a 1024-B ckv row
 constexpr int kKpeStride = 144;       // smem pitch of a 128-B kpe row
 constexpr int kCWarps = 4;            // consumer warps
-constexpr int kThreads = (kCWarps + 1) * 32;
+constexpr int kPWarps = 2;            // producer warps
+constexpr int kThreads = (kCWarps + kPWarps) * 32;
 constexpr int kPartFloats = kHeads * kDc + 2 * kHeads;  // acc[16][512], m[16], l[16]
 
 struct AttnParams {
@@ -72,10 +73,9 @@ struct AttnSmem {
   uint8_t ckv[NST][kRows * kCkvStride];
   uint8_t kpe[NST][kRows * kKpeStride];
   float4 sred[2][kCWarps][4][32];  // [buf][warp][n-block][lane]: conflict-free
-  uint32_t vmask[NST];
+  uint32_t vmask[NST][kPWarps];  // valid-row bits, one word per producer warp
   uint64_t full[NST];
   uint64_t empty[NST];
-  int last_flag;
 };
 
 __device__ __forceinline__ int cta_start(const AttnParams& p, int c) {
@@ -93,17 +93,22 @@ __device__ __forceinline__ float* part_slot(const AttnParams& p, int c, int v) {
 }
 
 // ------------------------------------------------------------------ producer
+// Producer warp pw gathers rows pw*16 .. pw*16+15 of every tile: each
+// 1024-B ckv row is one bulk copy (lanes 0-15), the 128-B kpe rows are
+// 16-byte cp.async chunks spread over all 32 lanes (4 per lane), so the copy
+// engine sees one operation per row and two warps issue in parallel.
 template <int NST>
-__device__ __forceinline__ void attn_producer(const AttnParams& p, AttnSmem<NST>& S, int lane,
-                                              int tile_begin, int tile_end) {
+__device__ __forceinline__ void attn_producer(const AttnParams& p, AttnSmem<NST>& S, int pw,
+                                              int lane, int tile_begin, int tile_end) {
+  constexpr int RPW = kRows / kPWarps;  // 16 rows per producer warp
   // Indices are fetched kIdxAhead tiles before use so that the dependent
   // global load is off the critical path of the row copies.
   constexpr int kIdxAhead = 3;
   auto load_idx = [&](int tile) -> int32_t {
-    if (tile >= tile_end) return -1;
+    if (tile >= tile_end || lane >= RPW) return -1;
     const int v = tile / p.tiles_per_token;
     const int t = v / p.head_groups;
-    const int r0 = (tile - v * p.tiles_per_token) * kRows;
+    const int r0 = (tile - v * p.tiles_per_token) * kRows + pw * RPW;
     return __ldg(p.idx + (int64_t)t * p.idx_st + r0 + lane);
   };
   int32_t ring[kIdxAhead];
@@ -121,91 +126,94 @@ __device__ __forceinline__ void attn_producer(const AttnParams& p, AttnSmem<NST>
       set_error(p.err, kErrTimeout);
       break;
     }
-    const bool valid = id >= 0 && id < p.num_slots;
-    if (id < -1 || id >= p.num_slots) set_error(p.err, kErrBadIndex);
+    const bool mine = lane < RPW;
+    const bool valid = mine && id >= 0 && id < p.num_slots;
+    if (mine && (id < -1 || id >= p.num_slots)) set_error(p.err, kErrBadIndex);
     const uint32_t mask = __ballot_sync(0xffffffffu, valid);
-    if (!valid) {
+    const int row = pw * RPW + lane;
+    if (mine && !valid) {
       // padding row: zeros, so 0-probability rows contribute exactly 0 to PV
-      float4* d = reinterpret_cast<float4*>(S.ckv[s] + lane * kCkvStride);
+      float4* d = reinterpret_cast<float4*>(S.ckv[s] + row * kCkvStride);
 #pragma unroll 8
       for (int k = 0; k < 64; ++k) d[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-      float4* e = reinterpret_cast<float4*>(S.kpe[s] + lane * kKpeStride);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) e[k] = make_float4(0.f, 0.f, 0.f, 0.f);
       fence_proxy_async_smem();
     }
-    if (lane == 0) S.vmask[s] = mask;
+    if (lane == 0) S.vmask[s][pw] = mask << (pw * RPW);
     __syncwarp();
-    if (lane == 0) mbar_arrive_expect_tx(&S.full[s], __popc(mask) * (kDc * 2 + kDp * 2));
+    if (lane == 0) mbar_arrive_expect_tx(&S.full[s], __popc(mask) * (kDc * 2));
     __syncwarp();
     if (valid) {
       const int64_t page = id >> 6, r = id & 63;
-      bulk_g2s(S.ckv[s] + lane * kCkvStride, p.ckv + page * p.ckv_sp + r * p.ckv_sr, kDc * 2,
-               &S.full[s]);
-      bulk_g2s(S.kpe[s] + lane * kKpeStride, p.kpe + page * p.kpe_sp + r * p.kpe_sr, kDp * 2,
+      bulk_g2s(S.ckv[s] + row * kCkvStride, p.ckv + page * p.ckv_sp + r * p.ckv_sr, kDc * 2,
                &S.full[s]);
     }
+    // kpe: chunk q = lane + 32*j of this warp's 16 rows x 8 chunks
+    const uint32_t kpe_s = smem_u32(S.kpe[s]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int q = lane + 32 * j, rr = q >> 3, ch = q & 7;
+      const int32_t rid = __shfl_sync(0xffffffffu, id, rr);
+      const bool ok = (mask >> rr) & 1u;
+      const int64_t page = ok ? (rid >> 6) : 0, r = ok ? (rid & 63) : 0;
+      const char* src = reinterpret_cast<const char*>(p.kpe + page * p.kpe_sp + r * p.kpe_sr) + ch * 16;
+      cp_async16(kpe_s + (pw * RPW + rr) * kKpeStride + ch * 16, src, ok ? 16u : 0u);
+    }
+    cp_async_arrive_noinc(&S.full[s]);
   }
   // Do not leave while copies issued by this warp may still be landing.
   for (int k = it > NST ? it - NST : 0; k < it; ++k) mbar_wait(&S.full[k % NST], (k / NST) & 1);
 }
 
 // ------------------------------------------------------------------ merge
-// LSE merge of the partial (acc, m, l) of every CTA that worked on virtual
-// token v (kernel.py:437-493), done by the 128 consumer threads of the CTA
-// that finished last.  Thread i owns output columns 4i..4i+3 of all 16 heads.
-__device__ __noinline__ void attn_merge(const AttnParams& p, int v, int c_first, int c_last) {
-  const int i = threadIdx.x;  // 0..127
-  float M[kHeads], L[kHeads];
+// LSE merge of the split-K partials (kernel.py:437-493 / the 3-phase merge
+// of :583-704 done in one pass): one CTA per (virtual token, head), launched
+// as a programmatic dependent of the attention grid so that its launch
+// overlaps the attention tail; all SMs merge in parallel.  Thread i owns
+// output columns 4i..4i+3; partials are read 8 at a time.
+__global__ void __launch_bounds__(128) dsa_attention_merge_kernel(const __grid_constant__ AttnParams p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // attention grid done, writes visible
+  const int h = blockIdx.x, v = blockIdx.y, i = threadIdx.x;
+  const int tpt = p.tiles_per_token;
+  const int c_first = cta_of_tile(p, v * tpt), c_last = cta_of_tile(p, v * tpt + tpt - 1);
+  if (c_first == c_last) return;  // written directly by the attention kernel
+  float M = -INFINITY;
+  for (int c = c_first; c <= c_last; ++c) M = fmaxf(M, __ldcg(part_slot(p, c, v) + kHeads * kDc + h));
+  float L = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int c0 = c_first; c0 <= c_last; c0 += 8) {
+    float4 a[8];
+    float w[8];
 #pragma unroll
-  for (int h = 0; h < kHeads; ++h) {
-    M[h] = -INFINITY;
-    L[h] = 0.f;
-  }
-  for (int c = c_first; c <= c_last; ++c) {
-    const float* pm = part_slot(p, c, v) + kHeads * kDc;
+    for (int u = 0; u < 8; ++u) {
+      w[u] = 0.f;
+      a[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (c0 + u <= c_last) {
+        const float* ps = part_slot(p, c0 + u, v);
+        const float m = __ldcg(ps + kHeads * kDc + h);
+        a[u] = __ldcg(reinterpret_cast<const float4*>(ps + h * kDc) + i);
+        if (m != -INFINITY) {
+          w[u] = exp2f(m - M);
+          L += w[u] * __ldcg(ps + kHeads * kDc + kHeads + h);
+        }
+      }
+    }
 #pragma unroll
-    for (int h = 0; h < kHeads; ++h) M[h] = fmaxf(M[h], __ldcg(pm + h));
-  }
-  float4 acc[kHeads];
-#pragma unroll
-  for (int h = 0; h < kHeads; ++h) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int c = c_first; c <= c_last; ++c) {
-    const float* ps = part_slot(p, c, v);
-#pragma unroll
-    for (int h = 0; h < kHeads; ++h) {
-      const float m = __ldcg(ps + kHeads * kDc + h);
-      const float l = __ldcg(ps + kHeads * kDc + kHeads + h);
-      const float w = (m == -INFINITY) ? 0.f : exp2f(m - M[h]);
-      L[h] += w * l;
-      const float4 a = __ldcg(reinterpret_cast<const float4*>(ps + h * kDc) + i);
-      acc[h].x += w * a.x;
-      acc[h].y += w * a.y;
-      acc[h].z += w * a.z;
-      acc[h].w += w * a.w;
+    for (int u = 0; u < 8; ++u) {
+      acc.x += w[u] * a[u].x;
+      acc.y += w[u] * a[u].y;
+      acc.z += w[u] * a[u].z;
+      acc.w += w[u] * a[u].w;
     }
   }
   const int t = v / p.head_groups, grp = v - t * p.head_groups;
-#pragma unroll
-  for (int h = 0; h < kHeads; ++h) {
-    const float inv = (M[h] == -INFINITY) ? 0.f : 1.f / L[h];
-    uint2 pk;
-    pk.x = pack_bf16(acc[h].x * inv, acc[h].y * inv);
-    pk.y = pack_bf16(acc[h].z * inv, acc[h].w * inv);
-    *reinterpret_cast<uint2*>(p.out + t * p.out_st + (int64_t)(grp * kHeads + h) * p.out_sh +
-                              4 * i) = pk;
-  }
-  if (i < kHeads) {
-    float m = M[0], l = L[0];
-#pragma unroll
-    for (int h = 1; h < kHeads; ++h)
-      if (h == i) {
-        m = M[h];
-        l = L[h];
-      }
-    p.lse[t * p.lse_st + (int64_t)(grp * kHeads + i) * p.lse_sh] =
-        (m == -INFINITY) ? -INFINITY : m + log2f(l);
-  }
+  const float inv = (M == -INFINITY) ? 0.f : 1.f / L;
+  uint2 pk;
+  pk.x = pack_bf16(acc.x * inv, acc.y * inv);
+  pk.y = pack_bf16(acc.z * inv, acc.w * inv);
+  *reinterpret_cast<uint2*>(p.out + t * p.out_st + (int64_t)(grp * kHeads + h) * p.out_sh + 4 * i) = pk;
+  if (i == 0)
+    p.lse[t * p.lse_st + (int64_t)(grp * kHeads + h) * p.lse_sh] =
+        (M == -INFINITY) ? -INFINITY : M + log2f(L);
 }
 
 // ------------------------------------------------------------------ kernel
@@ -220,15 +228,15 @@ __global__ void __launch_bounds__(kThreads, (NST == 2 ? 2 : 1)) dsa_attention_ke
   if (threadIdx.x == 0) {
 #pragma unroll
     for (int s = 0; s < NST; ++s) {
-      mbar_init(&S.full[s], 1);
+      mbar_init(&S.full[s], kPWarps * 33);  // per producer: expect_tx arrive + 32 cp.async arrivals
       mbar_init(&S.empty[s], kCWarps);
     }
     fence_mbar_init();
   }
   __syncthreads();
 
-  if (warp == kCWarps) {
-    attn_producer<NST>(p, S, lane, tile_begin, tile_end);
+  if (warp >= kCWarps) {
+    attn_producer<NST>(p, S, warp - kCWarps, lane, tile_begin, tile_end);
     return;
   }
 
@@ -318,7 +326,9 @@ __global__ void __launch_bounds__(kThreads, (NST == 2 ? 2 : 1)) dsa_attention_ke
       buf ^= 1;
 
       // ---- online softmax (base 2), rows g and g+8
-      const uint32_t vm = S.vmask[s];
+      uint32_t vm = 0;
+#pragma unroll
+      for (int q = 0; q < kPWarps; ++q) vm |= S.vmask[s][q];
       float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
       for (int nb = 0; nb < 4; ++nb) {
@@ -424,20 +434,11 @@ __global__ void __launch_bounds__(kThreads, (NST == 2 ? 2 : 1)) dsa_attention_ke
         __stcg(ps + kHeads * kDc + kHeads + g, l0);
         __stcg(ps + kHeads * kDc + kHeads + g + 8, l1);
       }
-      __threadfence();
-      named_bar_sync(1, kCWarps * 32);
-      if (threadIdx.x == 0) {
-        const int old = atomicAdd(p.counters + v, 1);
-        S.last_flag = (old == c_last - c_first);
-      }
-      named_bar_sync(1, kCWarps * 32);
-      if (S.last_flag) {
-        __threadfence();
-        attn_merge(p, v, c_first, c_last);
-        if (threadIdx.x == 0) p.counters[v] = 0;  // leave the counter ready for the next call
-      }
     }
   }
+  // This CTA's results are written: the merge grid (launched as a dependent)
+  // may start its prologue; it still waits for this whole grid to finish.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // ------------------------------------------------------------------ host side
@@ -657,6 +658,20 @@ int dsa_sparse_attention(const void* q_nope, int64_t q_nope_stride_token, int64_
   cudaError_t e = nst == 2 ? launch<2>(p, pl.ctas, st)
                            : nst == 3 ? launch<3>(p, pl.ctas, st) : launch<4>(p, pl.ctas, st);
   if (e != cudaSuccess) return fail(DSA_ERR_CUDA, cudaGetErrorString(e));
+  if (pl.ctas > 1) {  // tokens split across CTAs: merge grid as a programmatic dependent
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kHeads, (unsigned)pl.vtokens);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, dsa_attention_merge_kernel, p);
+    if (e != cudaSuccess) return fail(DSA_ERR_CUDA, cudaGetErrorString(e));
+  }
   return DSA_OK;
 }
 
