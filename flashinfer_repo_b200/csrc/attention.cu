@@ -177,7 +177,14 @@ __global__ void __launch_bounds__(128) dsa_attention_merge_kernel(const __grid_c
   const int c_first = cta_of_tile(p, v * tpt), c_last = cta_of_tile(p, v * tpt + tpt - 1);
   if (c_first == c_last) return;  // written directly by the attention kernel
   float M = -INFINITY;
-  for (int c = c_first; c <= c_last; ++c) M = fmaxf(M, __ldcg(part_slot(p, c, v) + kHeads * kDc + h));
+  for (int c0 = c_first; c0 <= c_last; c0 += 8) {  // 8 independent loads per round trip
+    float m[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      m[u] = (c0 + u <= c_last) ? __ldcg(part_slot(p, c0 + u, v) + kHeads * kDc + h) : -INFINITY;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) M = fmaxf(M, m[u]);
+  }
   float L = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int c0 = c_first; c0 <= c_last; c0 += 8) {
@@ -190,10 +197,11 @@ __global__ void __launch_bounds__(128) dsa_attention_merge_kernel(const __grid_c
       if (c0 + u <= c_last) {
         const float* ps = part_slot(p, c0 + u, v);
         const float m = __ldcg(ps + kHeads * kDc + h);
+        const float l = __ldcg(ps + kHeads * kDc + kHeads + h);
         a[u] = __ldcg(reinterpret_cast<const float4*>(ps + h * kDc) + i);
         if (m != -INFINITY) {
           w[u] = exp2f(m - M);
-          L += w[u] * __ldcg(ps + kHeads * kDc + kHeads + h);
+          L += w[u] * l;
         }
       }
     }

@@ -11,6 +11,7 @@ tensors or a missing library raise.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 
 import torch
@@ -47,6 +48,7 @@ class _Workspace:
 
 
 _workspaces: dict[int, _Workspace] = {}
+_ws_size_cache: dict[tuple, int] = {}
 
 
 def workspace_for(device: torch.device) -> _Workspace:
@@ -117,11 +119,15 @@ def kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, *, outp
 
     with torch.cuda.device(device):
         stream = torch.cuda.current_stream(device)
-        nbytes = ctypes.c_size_t(0)
-        _lib.call("dsa_sparse_attention_workspace_size", num_tokens, heads, topk,
-                  ctypes.byref(nbytes))
-        ws = workspace_for(device).get(device, nbytes.value, num_tokens * (heads // NUM_HEADS),
-                                       stream)
+        # the plan (and so the size) also depends on the tuning knobs
+        key = (device.index, num_tokens, heads, topk, os.environ.get("DSA_ATTN_CTAS"),
+               os.environ.get("DSA_ATTN_MIN_TILES"), os.environ.get("DSA_ATTN_STAGES"))
+        nbytes = _ws_size_cache.get(key)
+        if nbytes is None:
+            n = ctypes.c_size_t(0)
+            _lib.call("dsa_sparse_attention_workspace_size", num_tokens, heads, topk, ctypes.byref(n))
+            nbytes = _ws_size_cache[key] = n.value
+        ws = workspace_for(device).get(device, nbytes, num_tokens * (heads // NUM_HEADS), stream)
         _lib.call(
             "dsa_sparse_attention",
             q_nope.data_ptr(), q_nope.stride(0), q_nope.stride(1),
