@@ -111,3 +111,27 @@ def indexer_topk(q_fp8, k_cache_fp8, k_scale, weights, seq_lens, block_table, to
     request / decode token)."""
     scores = indexer_scores(q_fp8, k_cache_fp8, k_scale, weights, seq_lens, block_table, **kw)
     return topk_select(scores, seq_lens, block_table, topk)
+
+
+def index_cache_append(keys, slot_ids, k_cache_fp8, k_scale, *, num_pages=None, k_page_stride=None,
+                       scale_page_stride=None, device_error=None):
+    """Quantise `keys` [N,128] (bf16) to e4m3 with a per-token scale max|k|/448
+    and write them at flat slot ids `slot_ids` [N] (-1 = skip) of the paged
+    index-key cache (k_cache_fp8 [P,64,128] + k_scale [P,64], or the page-packed
+    layout via byte strides)."""
+    assert keys.dtype == torch.bfloat16 and keys.shape[-1] == INDEX_HEAD_DIM and keys.is_cuda
+    keys = keys.contiguous()
+    slot_ids = slot_ids.to(torch.int32).contiguous()
+    kc = _u8(k_cache_fp8)
+    if num_pages is None:
+        num_pages = kc.shape[0]
+    if k_page_stride is None:
+        k_page_stride = kc.stride(0)
+    if scale_page_stride is None:
+        scale_page_stride = k_scale.stride(0) * 4
+    err_ptr = device_error.data_ptr() if device_error is not None else None
+    with torch.cuda.device(keys.device):
+        stream = torch.cuda.current_stream(keys.device).cuda_stream
+        _lib.call("dsa_index_cache_append", keys.data_ptr(), keys.shape[0], slot_ids.data_ptr(),
+                  kc.data_ptr(), int(k_page_stride), k_scale.data_ptr(), int(scale_page_stride),
+                  int(num_pages), err_ptr, ctypes.c_void_p(stream))

@@ -167,6 +167,20 @@ int dsa_indexer_topk(const void* q_fp8, const void* k_cache_fp8, int64_t k_page_
                      int32_t* slots, int* device_error, void* stream);
 
 /*
+ * Quantise new index keys and append them to the paged FP8 index-key cache
+ * read by dsa_indexer_scores (the reference only reads this format,
+ * solution/triton/indexer_kernel.py:163-201).  For token i with flat slot id
+ * slot_ids[i] (page*64+slot; -1 = skip): scale = max|k|/448 (1 for an all-zero
+ * row), 128 e4m3 bytes of k/scale (round to nearest even, saturating) at
+ * k_cache_fp8 + page*k_page_stride + slot*128 and the fp32 scale at
+ * k_scale + page*scale_page_stride + slot*4.  keys_bf16 is [num_tokens, 128].
+ */
+int dsa_index_cache_append(const void* keys_bf16, int64_t num_tokens, const int32_t* slot_ids,
+                           void* k_cache_fp8, int64_t k_page_stride, void* k_scale,
+                           int64_t scale_page_stride, int64_t num_pages, int* device_error,
+                           void* stream);
+
+/*
  * Read (and optionally clear) the device error word of a workspace.
  * Synchronises the stream.  *bits receives DSA_DEVERR_* flags.
  */

@@ -110,3 +110,19 @@ def topk(scores, seq_lens, block_table, k, nthreads=None):
     lib().oracle_topk(_p(scores), B, L, _p(sl), _p(bt), bt.shape[1], int(k), _p(pos), _p(slots),
                       _threads(nthreads))
     return pos, slots
+
+
+def index_cache_append(keys_bf16_bits, slot_ids, k_cache, scales):
+    """Restatement of the FP8 index-key writer (no reference counterpart: the
+    reference only reads this cache): per token scale = max|k|/448 in fp32
+    (1 for an all-zero row), e4m3 = round-to-nearest-even(k/scale), saturating.
+    Writes into k_cache [P,64,128] uint8 and scales [P,64] float32 in place."""
+    from flashinfer_repo_b200.workloads import bf16_bits_to_f32, f32_to_e4m3_bits
+    k = bf16_bits_to_f32(keys_bf16_bits).reshape(-1, 128)
+    for i, sid in enumerate(np.asarray(slot_ids)):
+        if sid < 0:
+            continue
+        amax = np.float32(np.abs(k[i]).max())
+        sc = np.float32(amax / np.float32(448.0)) if amax > 0 else np.float32(1.0)
+        k_cache[sid >> 6, sid & 63] = f32_to_e4m3_bits((k[i] / sc).astype(np.float32))
+        scales[sid >> 6, sid & 63] = sc
