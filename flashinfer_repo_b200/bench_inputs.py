@@ -125,3 +125,27 @@ def indexer_bytes(seq_lens, heads=64, topk=TOPK) -> int:
     ctx = int(seq_lens.sum().item())
     B = seq_lens.numel()
     return ctx * 132 + B * (heads * 128 + heads * 4 + topk * 8)
+
+
+def make_prefill_device(seed=0, device="cuda", queries=4096, ctx=65536, heads=16, topk=TOPK):
+    """BASELINE cfg5 (one sequence per GPU): `queries` query tokens at absolute
+    positions ctx-queries .. ctx-1, each selecting `topk` distinct positions
+    <= its own position (causal), over one request of `ctx` tokens with a
+    shuffled page table."""
+    g = _gen(seed, device)
+    npg = (ctx + PS - 1) // PS
+    perm = torch.randperm(npg, generator=g, device=device).to(torch.int64)
+    ckv = _randn_bf16((npg, PS, DC), g, device, 0.5)
+    kpe = _randn_bf16((npg, PS, DP), g, device, 0.5)
+    q_nope = _randn_bf16((queries, heads, DC), g, device)
+    q_pe = _randn_bf16((queries, heads, DP), g, device)
+    idx = torch.empty((queries, topk), dtype=torch.int32, device=device)
+    pos0 = ctx - queries
+    for r0 in range(0, queries, 256):  # random keys, causal mask, top-k -> distinct positions
+        r1 = min(queries, r0 + 256)
+        keys = torch.rand((r1 - r0, ctx), generator=g, device=device)
+        allowed = torch.arange(ctx, device=device)[None, :] <= (pos0 + torch.arange(r0, r1, device=device))[:, None]
+        keys = torch.where(allowed, keys, torch.full_like(keys, -1.0))
+        pos = keys.topk(topk, dim=1).indices
+        idx[r0:r1] = (perm[pos // PS] * PS + pos % PS).to(torch.int32)
+    return q_nope, q_pe, ckv, kpe, idx, SM_SCALE

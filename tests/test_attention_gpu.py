@@ -144,3 +144,14 @@ def test_full_size_cfg2_against_oracle(cuda_device):
                                        small_idx.cpu().numpy(), scale)
     assert_attention_close(out, lse, ref_out, ref_lse, "cfg2 full")
     assert read_device_error(cuda_device) == 0
+
+
+def test_causal_prefill_against_oracle(cuda_device):
+    """cfg5 shape at oracle-friendly size: 96 queries at the end of an
+    8192-token context, causal top-2048 (positions <= the query's own)."""
+    from flashinfer_repo_b200.bench_inputs import make_prefill_device
+    qn, qp, ckv, kpe, idx, scale = make_prefill_device(seed=4, device=cuda_device, queries=96, ctx=8192)
+    out, lse = kernel(qn, qp, ckv, kpe, idx, scale)
+    ref_out, ref_lse = O.dsa_attention(out_bits(qn), out_bits(qp), out_bits(ckv), out_bits(kpe),
+                                       idx.cpu().numpy(), scale)
+    assert_attention_close(out, lse, ref_out, ref_lse, "prefill")
