@@ -155,3 +155,17 @@ def test_causal_prefill_against_oracle(cuda_device):
     ref_out, ref_lse = O.dsa_attention(out_bits(qn), out_bits(qp), out_bits(ckv), out_bits(kpe),
                                        idx.cpu().numpy(), scale)
     assert_attention_close(out, lse, ref_out, ref_lse, "prefill")
+
+
+def test_tvm_ffi_entry_point(cuda_device):
+    """Called through the TVM-FFI global `flashinfer.kernel` (the reference's
+    CUDA binding slot), the operator returns the same result."""
+    pytest.importorskip("tvm_ffi")
+    from flashinfer_repo_b200.binding import register
+    f = register()
+    case = W.cfg1_case(0)
+    args = case_to_device(case, cuda_device)
+    out, lse = f(*args, case.sm_scale)
+    out, lse = torch.from_dlpack(out), torch.from_dlpack(lse)
+    ref_out, ref_lse = kernel(*args, case.sm_scale)
+    assert torch.equal(out, ref_out) and torch.equal(lse, ref_lse)

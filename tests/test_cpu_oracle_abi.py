@@ -130,3 +130,16 @@ def test_kernel_rejects_cpu_tensors_and_bad_shapes():
     bad[0] = bad[0][:, :, :256]
     with pytest.raises(AssertionError):
         kernel(*bad, case.sm_scale)
+
+
+def test_tvm_ffi_slot_registered_and_routes_to_kernel():
+    """The reference's empty `flashinfer.kernel` TVM-FFI slot is filled; CPU
+    tensors reach the operator and are refused (no CPU path)."""
+    pytest.importorskip("tvm_ffi")
+    from flashinfer_repo_b200.binding import register
+    f = register()
+    bf = torch.bfloat16
+    with pytest.raises(Exception, match="CUDA"):
+        f(torch.zeros(1, 16, 512, dtype=bf), torch.zeros(1, 16, 64, dtype=bf),
+          torch.zeros(2, 64, 512, dtype=bf), torch.zeros(2, 64, 64, dtype=bf),
+          torch.zeros(1, 2048, dtype=torch.int32), 0.1)
