@@ -663,10 +663,15 @@ int dsa_sparse_attention(const void* q_nope, int64_t q_nope_stride_token, int64_
   p.part = reinterpret_cast<float*>(ws + pl.part_off);
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = nst == 2 ? launch<2>(p, pl.ctas, st)
-                           : nst == 3 ? launch<3>(p, pl.ctas, st) : launch<4>(p, pl.ctas, st);
+  // Profiling knob DSA_ATTN_STAGE: 1 = attention grid only, 2 = merge grid
+  // only (on the partials of an earlier call with the same shapes); default both.
+  const int stage = env_int("DSA_ATTN_STAGE", 0);
+  cudaError_t e = cudaSuccess;
+  if (stage != 2)
+    e = nst == 2 ? launch<2>(p, pl.ctas, st)
+                 : nst == 3 ? launch<3>(p, pl.ctas, st) : launch<4>(p, pl.ctas, st);
   if (e != cudaSuccess) return fail(DSA_ERR_CUDA, cudaGetErrorString(e));
-  if (pl.ctas > 1) {  // tokens split across CTAs: merge grid as a programmatic dependent
+  if (pl.ctas > 1 && stage != 1) {  // tokens split across CTAs: merge grid as a programmatic dependent
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(kHeads, (unsigned)pl.vtokens);
     cfg.blockDim = dim3(128);
