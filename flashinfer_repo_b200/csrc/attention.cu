@@ -449,6 +449,405 @@ __global__ void __launch_bounds__(kThreads, (NST == 2 ? 2 : 1)) dsa_attention_ke
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// ================================================================== tcgen05 variant
+// Same operator, tiles of 64 rows, MMAs on the 5th-generation tensor cores:
+//   S^T[64 rows x 16 heads] = K[64 x 576] . Q^T      (M=64, N=16, K=576: 36 x K16)
+//   O^T[512 dims x 16 heads] += V^T[512 x 64] . P^T  (4 x M=128, N=16, K=64)
+// with S^T and O^T in TMEM.  The ckv tile is stored once, as 128-byte-swizzled
+// 64-dim panels: K-major for QK^T and read MN-major as V^T for PV.
+//   warps 0-3  softmax + epilogue (TMEM lanes 0-127): read S^T, online
+//              softmax (base 2; O rescaled in TMEM only when a head's maximum
+//              grows by more than 2^8), P^T (bf16) to shared memory, output
+//   warps 4-7  gather: 16-byte cp.async of each selected row into the swizzled
+//              panels (zero-fill for padding), queries at segment starts
+//   warp 8     tcgen05.alloc / MMA issue (one lane) / commits
+constexpr int kTcRows = 64;
+constexpr int kTcPanel = kTcRows * 128;  // 64 rows x 64 dims (bf16)
+constexpr int kTcTile = 9 * kTcPanel;    // ckv panels 0-7 + kpe panel 8
+constexpr int kTcQPanel = kHeads * 128;  // 16 heads x 64 dims
+constexpr int kTcQ = 9 * kTcQPanel;
+constexpr int kTcThreads = 9 * 32;
+constexpr int kTcO = 0, kTcS = 64;       // TMEM columns: O^T blocks 0-63, S^T buffers 64, 80
+
+struct __align__(1024) TcSmem {
+  uint8_t kv[2][kTcTile];
+  uint8_t q[2][kTcQ];
+  uint8_t p[2][2048];  // P^T [64 rows][16 heads], MN-major, 8x8 core matrices
+  float red[2][4][kHeads];
+  float lsum[4][kHeads];
+  unsigned long long vmask[2][4];
+  uint64_t kv_full[2], kv_empty[2], q_full[2], q_empty[2], s_full[2], s_empty[2], p_full[2];
+  uint64_t pv_done, o_empty;
+  uint32_t tmem_base;
+};
+
+__device__ __forceinline__ uint32_t tc_swz(int row, int chunk) {
+  return row * 128 + ((chunk ^ (row & 7)) << 4);
+}
+
+// Per-head reduction of v[16] over the warp: afterwards lane l holds the
+// result for head l>>1 (16 shuffles instead of 80).
+template <bool kMax>
+__device__ __forceinline__ float warp_reduce_heads(const float* v, int lane) {
+  auto op = [](float a, float b) { return kMax ? fmaxf(a, b) : a + b; };
+  float a[8], b4[4], c2[2], d;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const bool hi = lane & 16;
+    const float keep = hi ? v[i + 8] : v[i], send = hi ? v[i] : v[i + 8];
+    a[i] = op(keep, __shfl_xor_sync(0xffffffffu, send, 16));
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const bool hi = lane & 8;
+    const float keep = hi ? a[i + 4] : a[i], send = hi ? a[i] : a[i + 4];
+    b4[i] = op(keep, __shfl_xor_sync(0xffffffffu, send, 8));
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const bool hi = lane & 4;
+    const float keep = hi ? b4[i + 2] : b4[i], send = hi ? b4[i] : b4[i + 2];
+    c2[i] = op(keep, __shfl_xor_sync(0xffffffffu, send, 4));
+  }
+  {
+    const bool hi = lane & 2;
+    const float keep = hi ? c2[1] : c2[0], send = hi ? c2[0] : c2[1];
+    d = op(keep, __shfl_xor_sync(0xffffffffu, send, 2));
+  }
+  return op(d, __shfl_xor_sync(0xffffffffu, d, 1));
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    dsa_attention_tc_kernel(const __grid_constant__ AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  TcSmem& S = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                         ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cta = blockIdx.x;
+  const int tile_begin = cta_start(p, cta), tile_end = cta_start(p, cta + 1);
+  const int tpt = p.tiles_per_token;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&S.kv_full[i], 4 * 32 + 4);  // 128 cp.async arrivals + 4 mask arrivals
+      mbar_init(&S.kv_empty[i], 1);
+      mbar_init(&S.q_full[i], 4 * 32);
+      mbar_init(&S.q_empty[i], 1);
+      mbar_init(&S.s_full[i], 1);
+      mbar_init(&S.s_empty[i], 4);
+      mbar_init(&S.p_full[i], 4);
+    }
+    mbar_init(&S.pv_done, 1);
+    mbar_init(&S.o_empty, 4);
+    fence_mbar_init();
+  }
+  if (warp == 8) tmem_alloc(&S.tmem_base, 128);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = S.tmem_base;
+
+  if (warp >= 4 && warp < 8) {
+    // ---------------------------------------------------------------- gather
+    const int pw = warp - 4;
+    constexpr int kIdxAhead = 3;
+    auto load_idx = [&](int tile) -> int32_t {
+      if (tile >= tile_end || lane >= 16) return -1;
+      const int v = tile / tpt;
+      const int t = v / p.head_groups;
+      const int r = (tile - v * tpt) * kTcRows + pw * 16 + lane;
+      return __ldg(p.idx + (int64_t)t * p.idx_st + r);
+    };
+    int32_t ring[kIdxAhead];
+#pragma unroll
+    for (int k = 0; k < kIdxAhead; ++k) ring[k] = load_idx(tile_begin + k);
+    int it = 0, seg = 0;
+    bool ok = true;
+    for (int tile = tile_begin; tile < tile_end && ok; ++tile, ++it) {
+      const int v = tile / tpt;
+      if (tile == tile_begin || tile % tpt == 0) {  // queries of a new (token, group)
+        const int qb = seg & 1;
+        if (!mbar_wait(&S.q_empty[qb], ((seg >> 1) & 1) ^ 1)) {
+          set_error(p.err, kErrTimeout);
+          break;
+        }
+        const int t = v / p.head_groups, grp = v - t * p.head_groups;
+        const uint32_t qs = smem_u32(S.q[qb]);
+#pragma unroll
+        for (int k = 0; k < 9; ++k) {
+          const int e = lane + 32 * k, h = pw * 4 + e / 72, c = e % 72;
+          const __nv_bfloat16* src =
+              c < 64 ? p.q_nope + t * p.qn_st + (int64_t)(grp * kHeads + h) * p.qn_sh + c * 8
+                     : p.q_pe + t * p.qp_st + (int64_t)(grp * kHeads + h) * p.qp_sh + (c - 64) * 8;
+          cp_async16(qs + (c >> 3) * kTcQPanel + tc_swz(h, c & 7), src, 16u);
+        }
+        cp_async_arrive_noinc(&S.q_full[qb]);
+        ++seg;
+      }
+      const int s = it & 1;
+      const int32_t id = ring[0];
+#pragma unroll
+      for (int k = 0; k + 1 < kIdxAhead; ++k) ring[k] = ring[k + 1];
+      ring[kIdxAhead - 1] = load_idx(tile + kIdxAhead);
+      if (!mbar_wait(&S.kv_empty[s], ((it >> 1) & 1) ^ 1)) {
+        set_error(p.err, kErrTimeout);
+        ok = false;
+        break;
+      }
+      const bool mine = lane < 16;
+      const bool valid = mine && id >= 0 && id < p.num_slots;
+      if (mine && (id < -1 || id >= p.num_slots)) set_error(p.err, kErrBadIndex);
+      const uint32_t bits = __ballot_sync(0xffffffffu, valid) & 0xffffu;
+      const uint32_t kv = smem_u32(S.kv[s]);
+#pragma unroll 4
+      for (int rr = 0; rr < 16; ++rr) {
+        const int row = pw * 16 + rr;
+        const int32_t rid = __shfl_sync(0xffffffffu, id, rr);
+        const bool rv = (bits >> rr) & 1u;
+        const int64_t page = rv ? (rid >> 6) : 0, r6 = rv ? (rid & 63) : 0;
+        const char* crow = reinterpret_cast<const char*>(p.ckv + page * p.ckv_sp + r6 * p.ckv_sr);
+        const char* krow = reinterpret_cast<const char*>(p.kpe + page * p.kpe_sp + r6 * p.kpe_sr);
+        const uint32_t nb = rv ? 16u : 0u;
+        cp_async16(kv + (lane >> 3) * kTcPanel + tc_swz(row, lane & 7), crow + lane * 16, nb);
+        cp_async16(kv + ((lane + 32) >> 3) * kTcPanel + tc_swz(row, lane & 7), crow + (lane + 32) * 16,
+                   nb);
+        if (lane < 8) cp_async16(kv + 8 * kTcPanel + tc_swz(row, lane), krow + lane * 16, nb);
+      }
+      cp_async_arrive_noinc(&S.kv_full[s]);
+      if (lane == 0) {
+        S.vmask[s][pw] = (unsigned long long)bits << (16 * pw);
+        mbar_arrive(&S.kv_full[s]);
+      }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");  // nothing of this warp still landing
+  } else if (warp == 8) {
+    // ---------------------------------------------------------------- MMA issue
+    if (lane == 0) {
+      constexpr uint32_t id_qk = umma_idesc(1, 1, 0, 0, kTcRows, kHeads);
+      constexpr uint32_t id_pv = umma_idesc(1, 1, 1, 1, 128, kHeads);
+      bool ok = true;
+      // QK of the next tile and PV of the oldest finished softmax are issued
+      // as soon as each is ready (polled), so a stage is released right after
+      // its PV even while the next tile is still landing.
+      const int ntiles = tile_end - tile_begin;
+      int qk_next = 0, pv_next = 0;       // tile indices (relative) of the next QK / PV
+      int qk_seg = -1;
+      const long long t_start = clock64();
+      while (pv_next < ntiles && ok) {
+        bool progressed = false;
+        if (qk_next < ntiles && qk_next <= pv_next + 1) {  // at most 2 S buffers in use
+          const int tile = tile_begin + qk_next;
+          const bool first = (qk_next == 0) || (tile % tpt == 0);
+          const int s = qk_next & 1;
+          const int sg = first ? qk_seg + 1 : qk_seg;
+          if ((!first || mbar_try_wait(&S.q_full[sg & 1], (sg >> 1) & 1)) &&
+              mbar_try_wait(&S.kv_full[s], (qk_next >> 1) & 1) &&
+              mbar_try_wait(&S.s_empty[s], ((qk_next >> 1) & 1) ^ 1)) {
+            qk_seg = sg;
+            tc_fence_after();
+            const uint32_t kvb = smem_u32(S.kv[s]), qb = smem_u32(S.q[sg & 1]);
+#pragma unroll
+            for (int j = 0; j < 36; ++j)
+              umma_f16(tmem + kTcS + 16 * s,
+                       umma_desc(kvb + (j >> 2) * kTcPanel + (j & 3) * 32, 16, 1024, kSwizzle128B),
+                       umma_desc(qb + (j >> 2) * kTcQPanel + (j & 3) * 32, 16, 1024, kSwizzle128B),
+                       id_qk, j > 0 ? 1u : 0u);
+            umma_commit(&S.s_full[s]);
+            const bool last = (tile + 1 == tile_end) || ((tile + 1) % tpt == 0);
+            if (last) umma_commit(&S.q_empty[sg & 1]);
+            ++qk_next;
+            progressed = true;
+          }
+        }
+        if (pv_next < qk_next) {
+          const int tile = tile_begin + pv_next;
+          const bool first = (pv_next == 0) || (tile % tpt == 0);
+          // segment index of this tile: count segment starts up to it
+          const int sj = (tile / tpt) - (tile_begin / tpt);
+          const int pb = pv_next & 1;
+          if (mbar_try_wait(&S.p_full[pb], (pv_next >> 1) & 1) &&
+              (!(first && sj > 0) || mbar_try_wait(&S.o_empty, (sj - 1) & 1))) {
+            tc_fence_after();
+            const uint32_t kvb = smem_u32(S.kv[pv_next & 1]), pbuf = smem_u32(S.p[pb]);
+#pragma unroll
+            for (int blk = 0; blk < 4; ++blk)
+#pragma unroll
+              for (int ks = 0; ks < 4; ++ks)
+                umma_f16(tmem + kTcO + 16 * blk,
+                         umma_desc(kvb + 2 * blk * kTcPanel + ks * 2048, kTcPanel, 1024, kSwizzle128B),
+                         umma_desc(pbuf + ks * 256, 128, 1024, 0), id_pv, (ks > 0 || !first) ? 1u : 0u);
+            umma_commit(&S.kv_empty[pv_next & 1]);
+            umma_commit(&S.pv_done);
+            ++pv_next;
+            progressed = true;
+          }
+        }
+        if (!progressed && clock64() - t_start > kWaitBudgetCycles * 8) ok = false;
+      }
+      if (!ok) set_error(p.err, kErrTimeout);
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------------- softmax + epilogue
+    const int tid = threadIdx.x;  // 0..127 == TMEM lane
+    const int row = warp * 16 + lane;  // S^T row held by this thread (lanes 0-15)
+    float m_used[kHeads], lp[kHeads];
+    int it = 0, pv_seen = 0;
+    bool ok = true;
+    auto wait_pv = [&](int j) -> bool {  // PV of tile j (and all before) complete
+      while (pv_seen <= j) {
+        if (!mbar_wait(&S.pv_done, pv_seen & 1)) return false;
+        ++pv_seen;
+      }
+      return true;
+    };
+    for (int tile = tile_begin; tile < tile_end && ok; ++tile, ++it) {
+      const int v = tile / tpt;
+      const bool first = (tile == tile_begin) || (tile % tpt == 0);
+      const bool last = (tile + 1 == tile_end) || ((tile + 1) % tpt == 0);
+      if (first) {
+#pragma unroll
+        for (int h = 0; h < kHeads; ++h) {
+          m_used[h] = -INFINITY;
+          lp[h] = 0.f;
+        }
+      }
+      const int s = it & 1;
+      if (!mbar_wait(&S.s_full[s], (it >> 1) & 1) || !mbar_wait(&S.kv_full[s], (it >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float x[kHeads];
+      tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + kTcS + 16 * s, x);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.s_empty[s]);
+      const unsigned long long vm = S.vmask[s][0] | S.vmask[s][1] | S.vmask[s][2] | S.vmask[s][3];
+      const bool valid = lane < 16 && ((vm >> row) & 1ull);
+#pragma unroll
+      for (int h = 0; h < kHeads; ++h) x[h] = valid ? x[h] * p.scale_log2 : -INFINITY;
+      // tile maximum per head over the 64 rows
+      const float wm = warp_reduce_heads<true>(x, lane);
+      if ((lane & 1) == 0) S.red[it & 1][warp][lane >> 1] = wm;
+      named_bar_sync(1, 128);
+      float nm[kHeads];
+      bool grow = false;
+#pragma unroll
+      for (int h = 0; h < kHeads; ++h) {
+        const float mt = fmaxf(fmaxf(S.red[it & 1][0][h], S.red[it & 1][1][h]),
+                               fmaxf(S.red[it & 1][2][h], S.red[it & 1][3][h]));
+        nm[h] = fmaxf(m_used[h], mt);
+        grow |= (mt > m_used[h] + 8.f) || (m_used[h] == -INFINITY && mt != -INFINITY);
+      }
+      if (it > 0 && !wait_pv(it - 1)) {  // P buffer free; O settled before a rescale
+        ok = false;
+        break;
+      }
+      if (grow) {  // uniform over the 128 threads
+        float alpha[kHeads];
+#pragma unroll
+        for (int h = 0; h < kHeads; ++h) {
+          alpha[h] = (m_used[h] == -INFINITY) ? 0.f : exp2f(m_used[h] - nm[h]);
+          lp[h] *= alpha[h];
+          m_used[h] = nm[h];
+        }
+        if (!first) {
+          tc_fence_after();
+#pragma unroll
+          for (int blk = 0; blk < 4; ++blk) {
+            float o[kHeads];
+            const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16) + kTcO + 16 * blk;
+            tmem_ld16(ta, o);
+#pragma unroll
+            for (int h = 0; h < kHeads; ++h) o[h] *= alpha[h];
+            tmem_st16(ta, o);
+          }
+        }
+      }
+      uint32_t pk[8];
+#pragma unroll
+      for (int h = 0; h < kHeads; h += 2) {
+        const float p0 = (x[h] == -INFINITY) ? 0.f : exp2f(x[h] - m_used[h]);
+        const float p1 = (x[h + 1] == -INFINITY) ? 0.f : exp2f(x[h + 1] - m_used[h + 1]);
+        lp[h] += p0;
+        lp[h + 1] += p1;
+        pk[h >> 1] = pack_bf16(p0, p1);
+      }
+      if (lane < 16) {
+        uint8_t* pb = S.p[it & 1] + (row >> 3) * 128 + (row & 7) * 16;
+        *reinterpret_cast<uint4*>(pb) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *reinterpret_cast<uint4*>(pb + 1024) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.p_full[it & 1]);
+
+      if (last) {
+        // ------------------------------------------------------------ epilogue
+        const float wl = warp_reduce_heads<false>(lp, lane);
+        if ((lane & 1) == 0) S.lsum[warp][lane >> 1] = wl;
+        if (!wait_pv(it)) {
+          ok = false;
+          break;
+        }
+        named_bar_sync(1, 128);
+        tc_fence_after();
+        float L[kHeads];
+#pragma unroll
+        for (int h = 0; h < kHeads; ++h) L[h] = S.lsum[0][h] + S.lsum[1][h] + S.lsum[2][h] + S.lsum[3][h];
+        const int t = v / p.head_groups, grp = v - t * p.head_groups;
+        const int c_first = cta_of_tile(p, v * tpt), c_last = cta_of_tile(p, v * tpt + tpt - 1);
+        const bool direct = c_first == c_last;
+        float* ps = direct ? nullptr : part_slot(p, cta, v);
+#pragma unroll
+        for (int blk = 0; blk < 4; ++blk) {
+          float o[kHeads];
+          tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + kTcO + 16 * blk, o);
+          const int d = 128 * blk + tid;
+#pragma unroll
+          for (int h = 0; h < kHeads; ++h) {
+            if (direct) {
+              const float inv = (m_used[h] == -INFINITY) ? 0.f : 1.f / L[h];
+              p.out[t * p.out_st + (int64_t)(grp * kHeads + h) * p.out_sh + d] = __float2bfloat16_rn(o[h] * inv);
+            } else {
+              __stcg(ps + h * kDc + d, o[h]);
+            }
+          }
+        }
+        if (tid < kHeads) {
+          float m = m_used[0], l = L[0];
+#pragma unroll
+          for (int h = 1; h < kHeads; ++h)
+            if (h == tid) {
+              m = m_used[h];
+              l = L[h];
+            }
+          if (direct) {
+            p.lse[t * p.lse_st + (int64_t)(grp * kHeads + tid) * p.lse_sh] =
+                (m == -INFINITY) ? -INFINITY : m + log2f(l);
+          } else {
+            __stcg(ps + kHeads * kDc + tid, m);
+            __stcg(ps + kHeads * kDc + kHeads + tid, l);
+          }
+        }
+        tc_fence_before();
+        named_bar_sync(1, 128);  // lsum / O reads done before the next segment
+        if (lane == 0) mbar_arrive(&S.o_empty);
+      }
+    }
+    if (!ok) set_error(p.err, kErrTimeout);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
+  }
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ------------------------------------------------------------------ host side
 namespace {
 
@@ -536,14 +935,30 @@ struct Plan {
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 // Grid plan: an even split of all tiles over min(slots, tiles/min_tiles) CTAs.
-int make_plan(int64_t num_tokens, int64_t heads, int64_t topk, int nst, Plan* pl) {
+// Which kernel: DSA_ATTN_IMPL=0 (default) the mma.sync kernel (32-row tiles),
+// 1 the tcgen05 kernel (64-row tiles).  With 16 heads every tcgen05 MMA has
+// N=16 and a 64-row tile in MMA layout takes 72 KB of shared memory (two
+// stages fit), so on this pool's B200 the tcgen05 kernel measured slower on
+// both the HBM-bound decode (cfg2: 82 vs 53 us) and the L2-resident prefill
+// (cfg5: 3.2 vs 1.6 ms); it is kept as a tested alternative.
+int impl_choice() { return env_int("DSA_ATTN_IMPL", 0); }
+
+int tc_smem_bytes() { return (int)sizeof(TcSmem) + 1024; }
+
+int make_plan(int64_t num_tokens, int64_t heads, int64_t topk, int nst, Plan* pl, bool tc = false) {
   int sms = 0;
-  const int occ = device_slots(nst, &sms);
+  int occ = 0;
+  if (tc) {
+    occ = device_slots(2, &sms) > 0 ? 1 : 0;  // SM count; one tcgen05 CTA per SM
+  } else {
+    occ = device_slots(nst, &sms);
+  }
   if (occ < 1) return fail(DSA_ERR_CUDA, "cannot query device / occupancy for the attention kernel");
-  const int64_t tpt = topk / kRows;
+  const int64_t tpt = topk / (tc ? kTcRows : kRows);
   pl->vtokens = num_tokens * (heads / kHeads);
   pl->total_tiles = pl->vtokens * tpt;
-  const int min_tiles = env_int("DSA_ATTN_MIN_TILES", 4) > 0 ? env_int("DSA_ATTN_MIN_TILES", 4) : 1;
+  const int mt_env = env_int("DSA_ATTN_MIN_TILES", tc ? 2 : 4);
+  const int min_tiles = mt_env > 0 ? mt_env : 1;
   int64_t ctas = (int64_t)sms * occ;
   const int forced = env_int("DSA_ATTN_CTAS", 0);
   if (forced > 0) ctas = forced;
@@ -585,7 +1000,8 @@ int dsa_sparse_attention_workspace_size(int64_t num_tokens, int64_t num_heads, i
   if (num_tokens < 0 || num_heads <= 0 || num_heads % kHeads || topk <= 0 || topk % kRows)
     return fail(DSA_ERR_INVALID_ARG, "num_heads must be a multiple of 16 and topk of 32");
   Plan pl;
-  const int rc = make_plan(num_tokens > 0 ? num_tokens : 1, num_heads, topk, stages_choice(), &pl);
+  const bool tc = impl_choice() == 1 && topk % kTcRows == 0;
+  const int rc = make_plan(num_tokens > 0 ? num_tokens : 1, num_heads, topk, stages_choice(), &pl, tc);
   if (rc) return rc;
   *bytes = pl.bytes;
   return DSA_OK;
@@ -624,8 +1040,13 @@ int dsa_sparse_attention(const void* q_nope, int64_t q_nope_stride_token, int64_
   if ((reinterpret_cast<uintptr_t>(output) & 7) || out_stride_token % 4 || out_stride_head % 4)
     return fail(DSA_ERR_INVALID_ARG, "output rows must be 8-byte aligned");
   const int nst = stages_choice();
+  // the tcgen05 kernel gathers queries with 16-byte copies
+  const bool q16 = !(reinterpret_cast<uintptr_t>(q_nope) & 15) && !(reinterpret_cast<uintptr_t>(q_pe) & 15) &&
+                   q_nope_stride_token % 8 == 0 && q_nope_stride_head % 8 == 0 &&
+                   q_pe_stride_token % 8 == 0 && q_pe_stride_head % 8 == 0;
+  const bool tc = impl_choice() == 1 && topk % kTcRows == 0 && q16;
   Plan pl;
-  int rc = make_plan(num_tokens, num_heads, topk, nst, &pl);
+  int rc = make_plan(num_tokens, num_heads, topk, nst, &pl, tc);
   if (rc) return rc;
   if (workspace_bytes < pl.bytes || (reinterpret_cast<uintptr_t>(workspace) & 255))
     return fail(DSA_ERR_WORKSPACE, "workspace too small or not 256-byte aligned");
@@ -653,7 +1074,7 @@ int dsa_sparse_attention(const void* q_nope, int64_t q_nope_stride_token, int64_
   p.lse_sh = lse_stride_head;
   p.num_slots = num_pages * 64;
   p.head_groups = (int)(num_heads / kHeads);
-  p.tiles_per_token = (int)(topk / kRows);
+  p.tiles_per_token = (int)(topk / (tc ? kTcRows : kRows));
   p.scale_log2 = sm_scale * 1.4426950408889634f;
   p.tiles_base = pl.base;
   p.tiles_rem = pl.rem;
@@ -667,9 +1088,19 @@ int dsa_sparse_attention(const void* q_nope, int64_t q_nope_stride_token, int64_
   // only (on the partials of an earlier call with the same shapes); default both.
   const int stage = env_int("DSA_ATTN_STAGE", 0);
   cudaError_t e = cudaSuccess;
-  if (stage != 2)
-    e = nst == 2 ? launch<2>(p, pl.ctas, st)
-                 : nst == 3 ? launch<3>(p, pl.ctas, st) : launch<4>(p, pl.ctas, st);
+  if (stage != 2) {
+    if (tc) {
+      e = cudaFuncSetAttribute(dsa_attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               tc_smem_bytes());
+      if (e == cudaSuccess) {
+        dsa_attention_tc_kernel<<<pl.ctas, kTcThreads, tc_smem_bytes(), st>>>(p);
+        e = cudaGetLastError();
+      }
+    } else {
+      e = nst == 2 ? launch<2>(p, pl.ctas, st)
+                   : nst == 3 ? launch<3>(p, pl.ctas, st) : launch<4>(p, pl.ctas, st);
+    }
+  }
   if (e != cudaSuccess) return fail(DSA_ERR_CUDA, cudaGetErrorString(e));
   if (pl.ctas > 1 && stage != 1) {  // tokens split across CTAs: merge grid as a programmatic dependent
     cudaLaunchConfig_t cfg = {};

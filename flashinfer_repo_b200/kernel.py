@@ -121,7 +121,8 @@ def kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, *, outp
         stream = torch.cuda.current_stream(device)
         # the plan (and so the size) also depends on the tuning knobs
         key = (device.index, num_tokens, heads, topk, os.environ.get("DSA_ATTN_CTAS"),
-               os.environ.get("DSA_ATTN_MIN_TILES"), os.environ.get("DSA_ATTN_STAGES"))
+               os.environ.get("DSA_ATTN_MIN_TILES"), os.environ.get("DSA_ATTN_STAGES"),
+               os.environ.get("DSA_ATTN_IMPL"))
         nbytes = _ws_size_cache.get(key)
         if nbytes is None:
             n = ctypes.c_size_t(0)

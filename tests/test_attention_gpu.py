@@ -21,7 +21,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 @pytest.fixture(autouse=True)
 def _env_guard(monkeypatch):
-    for k in ("DSA_ATTN_CTAS", "DSA_ATTN_STAGES", "DSA_ATTN_MIN_TILES"):
+    for k in ("DSA_ATTN_CTAS", "DSA_ATTN_STAGES", "DSA_ATTN_MIN_TILES", "DSA_ATTN_IMPL"):
         monkeypatch.delenv(k, raising=False)
     yield
 
@@ -169,3 +169,25 @@ def test_tvm_ffi_entry_point(cuda_device):
     out, lse = torch.from_dlpack(out), torch.from_dlpack(lse)
     ref_out, ref_lse = kernel(*args, case.sm_scale)
     assert torch.equal(out, ref_out) and torch.equal(lse, ref_lse)
+
+
+@pytest.mark.parametrize("name", list(CASES))
+def test_tcgen05_variant_golden(cuda_device, monkeypatch, name):
+    """The tcgen05 kernel (64-row tiles, TMEM accumulators) on the reference's
+    golden outputs."""
+    monkeypatch.setenv("DSA_ATTN_IMPL", "1")
+    case = CASES[name]()
+    g = np.load(os.path.join(HERE, "golden", f"attn_{name}.npz"))
+    out, lse = kernel(*case_to_device(case, cuda_device), case.sm_scale)
+    assert_attention_close(out, lse, g["out"], g["lse"], name)
+
+
+@pytest.mark.parametrize("ctas", ["1", "5", "64"])
+def test_tcgen05_variant_ragged_and_splits(cuda_device, monkeypatch, ctas):
+    monkeypatch.setenv("DSA_ATTN_IMPL", "1")
+    monkeypatch.setenv("DSA_ATTN_CTAS", ctas)
+    monkeypatch.setenv("DSA_ATTN_MIN_TILES", "1")
+    case = W.make_attention_case(15, [5000, 300, 3000, 64, 9000, 2048])
+    case.idx[2, 100:900] = -1
+    case.idx[3, :] = -1
+    _oracle_check(case, cuda_device)
