@@ -447,15 +447,16 @@ def run_cfg4(args):
 
 def run_cfg3(args):
     """BASELINE cfg3: T=8 tokens, 128 heads, context 131072, clustered top-k,
-    latent cache replicated on every GPU; heads sharded 128/N per rank and the
-    outputs all-gathered (NCCL).  Strong scaling: the job is fixed."""
+    latent cache replicated on every GPU; heads sharded 128/N per rank, each
+    rank's epilogues storing its heads into every rank's output over NVLink
+    (peer barrier after); the NCCL all-gather variant is timed beside it.  Strong scaling: the job is fixed."""
     rank, world, local = dist_setup(args.gpus)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     import torch.distributed as dist
     from flashinfer_repo_b200 import kernel
     from flashinfer_repo_b200.bench_inputs import attention_bytes, make_cfg3_device
-    from flashinfer_repo_b200.parallel import head_sharded_attention
+    from flashinfer_repo_b200.parallel import PeerHeadShardedAttention, head_sharded_attention
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
     qn, qp, ckv, kpe, idx, scale = make_cfg3_device(seed=3000, device=dev)  # same on every rank
@@ -465,15 +466,34 @@ def run_cfg3(args):
     stream = torch.cuda.current_stream(dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
-    def step():
+    peer = PeerHeadShardedAttention(T, H, dev) if world > 1 else None
+
+    def step():  # fused: epilogues store into every rank's output, one peer barrier
         if world > 1:
-            return head_sharded_attention(qn, qp, ckv, kpe, idx, scale)
+            return peer(qn, qp, ckv, kpe, idx, scale)
         return kernel(qn, qp, ckv, kpe, idx, scale)
+
+    def step_allgather():  # unfused: 16-head kernel, pack, NCCL all-gather, unpack
+        return head_sharded_attention(qn, qp, ckv, kpe, idx, scale)
     for _ in range(args.warmup):
         step()
+        if world > 1:
+            step_allgather()
     torch.cuda.synchronize()
-    k_ms, s_ms = [], []
+    k_ms, s_ms, g_ms = [], [], []
     for i in range(args.steps):
+        if world > 1:  # the all-gather variant, for comparison (same L2 state)
+            flush.fill_(i & 0xFF)
+            dist.barrier()
+            torch.cuda.synchronize()
+            torch.cuda._sleep(200_000)
+            g0 = torch.cuda.Event(enable_timing=True)
+            g1 = torch.cuda.Event(enable_timing=True)
+            g0.record(stream)
+            step_allgather()
+            g1.record(stream)
+            g1.synchronize()
+            g_ms.append(g0.elapsed_time(g1))
         flush.fill_(i & 0xFF)
         e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
         e[0].record(stream)
@@ -491,10 +511,11 @@ def run_cfg3(args):
         e3.synchronize()
         k_ms.append(e[0].elapsed_time(e[1]))
         s_ms.append(e[2].elapsed_time(e3))
-    t = torch.tensor([statistics.median(k_ms), statistics.median(s_ms)], dtype=torch.float64, device=dev)
+    t = torch.tensor([statistics.median(k_ms), statistics.median(s_ms),
+                      statistics.median(g_ms) if g_ms else 0.0], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    kms, sms = t.tolist()
+    kms, sms, gms = t.tolist()
     peak, kind = peaks()
     if rank == 0:
         ab = attention_bytes(idx) * (h // 16)  # the 16-head operator's bytes per head group
@@ -504,17 +525,22 @@ def run_cfg3(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded, BASELINE cfg3 shapes and distributions)",
             "config": {"workload": "cfg3: T=8, 128 heads, ctx 131072, clustered top-2048",
-                       "parallelism": f"heads {h}/rank x {world} + all-gather",
+                       "parallelism": f"heads {h}/rank x {world}" + (
+                           ", outputs stored into every rank's buffer by the epilogues + peer barrier"
+                           if world > 1 else ""),
                        "l2": "flushed before every step (256 MiB write, untimed)"},
-            "kernel_ms": kms, "step_ms_incl_allgather": sms,
+            "kernel_ms": kms, "step_ms_fused_gather": sms,
+            "step_ms_nccl_allgather": gms if world > 1 else None,
             "roofline": {"bound": "hbm", "kernel": "dsa_attention_kernel",
                          "achieved": ab / (kms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
                          "frac": ab / (kms / 1e3) / 1e9 / peak, "traffic": None,
                          "note": "algorithmic bytes per rank = 16-head operator bytes x head groups "
                                  "(repeat row reads of the groups are served from L2)"},
-            "gpu_launches": args.steps * 2,
+            "gpu_launches": args.steps * (3 if world > 1 else 2),  # attention + merge (+ peer barrier)
         }), flush=True)
     if world > 1:
+        dist.barrier()
+        peer.close()
         dist.destroy_process_group()
 
 

@@ -25,6 +25,14 @@ SIGNATURES = {
                              I64, I64, I64, I64, I64, F32, P, I64, I64, P, I64, I64, P, SZ, P],
     "dsa_sparse_attention_noalloc": [P, I64, I64, P, I64, I64, P, I64, I64, P, I64, I64, P, I64,
                                      I64, I64, I64, I64, I64, F32, P, I64, I64, P, I64, I64, P],
+    "dsa_sparse_attention_scatter": [P, I64, I64, P, I64, I64, P, I64, I64, P, I64, I64, P, I64,
+                                     I64, I64, I64, I64, I64, F32, P, I64, I64, P, I64, I64, INT,
+                                     P, SZ, P],
+    "dsa_peer_alloc": [SZ, ctypes.POINTER(P), P],
+    "dsa_peer_open": [P, ctypes.POINTER(P)],
+    "dsa_peer_close": [P],
+    "dsa_peer_free": [P],
+    "dsa_peer_barrier": [P, INT, INT, P, P],
     "dsa_read_device_error": [P, INT, ctypes.POINTER(INT), P],
     "dsa_indexer_scores": [P, P, I64, P, I64, P, P, I64, P, I64, I64, I64, I64, I64, P, I64, P, P],
     "dsa_index_cache_append": [P, I64, P, P, I64, P, I64, I64, P, P],

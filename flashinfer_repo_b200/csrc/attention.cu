@@ -36,6 +36,7 @@
 namespace dsa {
 
 constexpr int kHeads = 16;
+constexpr int kMaxTargets = 8;  // output targets of the scatter entry (GPUs of one node)
 constexpr int kDc = 512;
 constexpr int kDp = 64;
 constexpr int kRows = 32;             // rows per tile
@@ -63,6 +64,13 @@ struct AttnParams {
   int tiles_per_token;  // topk / 32
   float scale_log2;     // sm_scale * log2(e)
   int tiles_base, tiles_rem;
+  // Optional extra output targets (fused all-gather of head-sharded outputs):
+  // when n_peers > 0, every output / lse store goes to each of the n_peers
+  // bases (peer GPUs' buffers over NVLink, this rank's head slice), with the
+  // same strides; out / lse are then unused.
+  __nv_bfloat16* out_peers[kMaxTargets];
+  float* lse_peers[kMaxTargets];
+  int n_peers;
   float* part;
   int* counters;
   int* err;
@@ -90,6 +98,14 @@ __device__ __forceinline__ int cta_of_tile(const AttnParams& p, int tile) {
 __device__ __forceinline__ float* part_slot(const AttnParams& p, int c, int v) {
   const int j = (v == cta_start(p, c) / p.tiles_per_token) ? 0 : 1;
   return p.part + (int64_t)(2 * c + j) * kPartFloats;
+}
+
+__device__ __forceinline__ int n_targets(const AttnParams& p) { return p.n_peers > 0 ? p.n_peers : 1; }
+__device__ __forceinline__ __nv_bfloat16* out_target(const AttnParams& p, int k) {
+  return p.n_peers > 0 ? p.out_peers[k] : p.out;
+}
+__device__ __forceinline__ float* lse_target(const AttnParams& p, int k) {
+  return p.n_peers > 0 ? p.lse_peers[k] : p.lse;
 }
 
 // ------------------------------------------------------------------ producer
@@ -218,10 +234,13 @@ __global__ void __launch_bounds__(128) dsa_attention_merge_kernel(const __grid_c
   uint2 pk;
   pk.x = pack_bf16(acc.x * inv, acc.y * inv);
   pk.y = pack_bf16(acc.z * inv, acc.w * inv);
-  *reinterpret_cast<uint2*>(p.out + t * p.out_st + (int64_t)(grp * kHeads + h) * p.out_sh + 4 * i) = pk;
-  if (i == 0)
-    p.lse[t * p.lse_st + (int64_t)(grp * kHeads + h) * p.lse_sh] =
-        (M == -INFINITY) ? -INFINITY : M + log2f(L);
+  for (int k = 0; k < n_targets(p); ++k) {
+    *reinterpret_cast<uint2*>(out_target(p, k) + t * p.out_st + (int64_t)(grp * kHeads + h) * p.out_sh +
+                              4 * i) = pk;
+    if (i == 0)
+      lse_target(p, k)[t * p.lse_st + (int64_t)(grp * kHeads + h) * p.lse_sh] =
+          (M == -INFINITY) ? -INFINITY : M + log2f(L);
+  }
 }
 
 // ------------------------------------------------------------------ kernel
@@ -414,19 +433,21 @@ __global__ void __launch_bounds__(kThreads, (NST == 2 ? 2 : 1)) dsa_attention_ke
     if (c_first == c_last) {
       const float i0 = (m0 == -INFINITY) ? 0.f : 1.f / l0;
       const float i1 = (m1 == -INFINITY) ? 0.f : 1.f / l1;
-      __nv_bfloat16* o0 = p.out + t * p.out_st + (int64_t)(grp * kHeads + g) * p.out_sh;
-      __nv_bfloat16* o1 = o0 + 8 * p.out_sh;
+      for (int k = 0; k < n_targets(p); ++k) {
+        __nv_bfloat16* o0 = out_target(p, k) + t * p.out_st + (int64_t)(grp * kHeads + g) * p.out_sh;
+        __nv_bfloat16* o1 = o0 + 8 * p.out_sh;
 #pragma unroll
-      for (int nb = 0; nb < 16; ++nb) {
-        const int d = 128 * warp + 8 * nb + 2 * c;
-        *reinterpret_cast<uint32_t*>(o0 + d) = pack_bf16(o[nb][0] * i0, o[nb][1] * i0);
-        *reinterpret_cast<uint32_t*>(o1 + d) = pack_bf16(o[nb][2] * i1, o[nb][3] * i1);
-      }
-      if (warp == 0 && c == 0) {
-        float* lp = p.lse + t * p.lse_st;
-        lp[(int64_t)(grp * kHeads + g) * p.lse_sh] = (m0 == -INFINITY) ? -INFINITY : m0 + log2f(l0);
-        lp[(int64_t)(grp * kHeads + g + 8) * p.lse_sh] =
-            (m1 == -INFINITY) ? -INFINITY : m1 + log2f(l1);
+        for (int nb = 0; nb < 16; ++nb) {
+          const int d = 128 * warp + 8 * nb + 2 * c;
+          *reinterpret_cast<uint32_t*>(o0 + d) = pack_bf16(o[nb][0] * i0, o[nb][1] * i0);
+          *reinterpret_cast<uint32_t*>(o1 + d) = pack_bf16(o[nb][2] * i1, o[nb][3] * i1);
+        }
+        if (warp == 0 && c == 0) {
+          float* lp = lse_target(p, k) + t * p.lse_st;
+          lp[(int64_t)(grp * kHeads + g) * p.lse_sh] = (m0 == -INFINITY) ? -INFINITY : m0 + log2f(l0);
+          lp[(int64_t)(grp * kHeads + g + 8) * p.lse_sh] =
+              (m1 == -INFINITY) ? -INFINITY : m1 + log2f(l1);
+        }
       }
     } else {
       float* ps = part_slot(p, cta, v);
@@ -810,7 +831,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           for (int h = 0; h < kHeads; ++h) {
             if (direct) {
               const float inv = (m_used[h] == -INFINITY) ? 0.f : 1.f / L[h];
-              p.out[t * p.out_st + (int64_t)(grp * kHeads + h) * p.out_sh + d] = __float2bfloat16_rn(o[h] * inv);
+              const __nv_bfloat16 ov = __float2bfloat16_rn(o[h] * inv);
+              for (int k = 0; k < n_targets(p); ++k)
+                out_target(p, k)[t * p.out_st + (int64_t)(grp * kHeads + h) * p.out_sh + d] = ov;
             } else {
               __stcg(ps + h * kDc + d, o[h]);
             }
@@ -825,8 +848,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               l = L[h];
             }
           if (direct) {
-            p.lse[t * p.lse_st + (int64_t)(grp * kHeads + tid) * p.lse_sh] =
-                (m == -INFINITY) ? -INFINITY : m + log2f(l);
+            for (int k = 0; k < n_targets(p); ++k)
+              lse_target(p, k)[t * p.lse_st + (int64_t)(grp * kHeads + tid) * p.lse_sh] =
+                  (m == -INFINITY) ? -INFINITY : m + log2f(l);
           } else {
             __stcg(ps + kHeads * kDc + tid, m);
             __stcg(ps + kHeads * kDc + kHeads + tid, l);
@@ -990,24 +1014,7 @@ int report_error(int code, const char* msg) { return fail(code, msg); }
 
 using namespace dsa;
 
-extern "C" {
-
-const char* dsa_last_error_message(void) { return g_errmsg; }
-
-int dsa_sparse_attention_workspace_size(int64_t num_tokens, int64_t num_heads, int64_t topk,
-                                        size_t* bytes) {
-  if (!bytes) return fail(DSA_ERR_INVALID_ARG, "bytes is NULL");
-  if (num_tokens < 0 || num_heads <= 0 || num_heads % kHeads || topk <= 0 || topk % kRows)
-    return fail(DSA_ERR_INVALID_ARG, "num_heads must be a multiple of 16 and topk of 32");
-  Plan pl;
-  const bool tc = impl_choice() == 1 && topk % kTcRows == 0;
-  const int rc = make_plan(num_tokens > 0 ? num_tokens : 1, num_heads, topk, stages_choice(), &pl, tc);
-  if (rc) return rc;
-  *bytes = pl.bytes;
-  return DSA_OK;
-}
-
-int dsa_sparse_attention(const void* q_nope, int64_t q_nope_stride_token, int64_t q_nope_stride_head,
+static int attention_impl(const void* q_nope, int64_t q_nope_stride_token, int64_t q_nope_stride_head,
                          const void* q_pe, int64_t q_pe_stride_token, int64_t q_pe_stride_head,
                          const void* ckv_cache, int64_t ckv_stride_page, int64_t ckv_stride_row,
                          const void* kpe_cache, int64_t kpe_stride_page, int64_t kpe_stride_row,
@@ -1016,7 +1023,7 @@ int dsa_sparse_attention(const void* q_nope, int64_t q_nope_stride_token, int64_
                          int64_t topk, float sm_scale, void* output, int64_t out_stride_token,
                          int64_t out_stride_head, float* lse, int64_t lse_stride_token,
                          int64_t lse_stride_head, void* workspace, size_t workspace_bytes,
-                         void* stream) {
+                         void* stream, void* const* out_peers, float* const* lse_peers, int n_peers) {
   if (num_tokens < 0) return fail(DSA_ERR_INVALID_ARG, "num_tokens < 0");
   if (num_heads <= 0 || num_heads % kHeads)
     return fail(DSA_ERR_UNSUPPORTED, "num_heads must be a positive multiple of 16");
@@ -1026,6 +1033,14 @@ int dsa_sparse_attention(const void* q_nope, int64_t q_nope_stride_token, int64_
   if (num_pages < 0 || num_pages * 64 > INT32_MAX)
     return fail(DSA_ERR_INVALID_ARG, "num_pages out of range for int32 slot ids");
   if (num_tokens == 0) return DSA_OK;
+  if (n_peers > 0) {  // stores go to the targets; output / lse are unused
+    if (!out_peers || !lse_peers) return fail(DSA_ERR_INVALID_ARG, "NULL target pointer array");
+    for (int k = 0; k < n_peers; ++k)
+      if (!out_peers[k] || !lse_peers[k] || (reinterpret_cast<uintptr_t>(out_peers[k]) & 7))
+        return fail(DSA_ERR_INVALID_ARG, "output targets must be non-NULL and 8-byte aligned");
+    output = out_peers[0];
+    lse = lse_peers[0];
+  }
   if (!q_nope || !q_pe || !ckv_cache || !kpe_cache || !sparse_indices || !output || !lse ||
       !workspace)
     return fail(DSA_ERR_INVALID_ARG, "NULL pointer argument");
@@ -1059,6 +1074,11 @@ int dsa_sparse_attention(const void* q_nope, int64_t q_nope_stride_token, int64_
   p.idx = sparse_indices;
   p.out = static_cast<__nv_bfloat16*>(output);
   p.lse = lse;
+  p.n_peers = n_peers;
+  for (int k = 0; k < kMaxTargets; ++k) {
+    p.out_peers[k] = k < n_peers ? static_cast<__nv_bfloat16*>(out_peers[k]) : nullptr;
+    p.lse_peers[k] = k < n_peers ? lse_peers[k] : nullptr;
+  }
   p.qn_st = q_nope_stride_token;
   p.qn_sh = q_nope_stride_head;
   p.qp_st = q_pe_stride_token;
@@ -1117,6 +1137,63 @@ int dsa_sparse_attention(const void* q_nope, int64_t q_nope_stride_token, int64_
     if (e != cudaSuccess) return fail(DSA_ERR_CUDA, cudaGetErrorString(e));
   }
   return DSA_OK;
+}
+
+extern "C" {
+
+const char* dsa_last_error_message(void) { return g_errmsg; }
+
+int dsa_sparse_attention_workspace_size(int64_t num_tokens, int64_t num_heads, int64_t topk,
+                                        size_t* bytes) {
+  if (!bytes) return fail(DSA_ERR_INVALID_ARG, "bytes is NULL");
+  if (num_tokens < 0 || num_heads <= 0 || num_heads % kHeads || topk <= 0 || topk % kRows)
+    return fail(DSA_ERR_INVALID_ARG, "num_heads must be a multiple of 16 and topk of 32");
+  Plan pl;
+  const bool tc = impl_choice() == 1 && topk % kTcRows == 0;
+  const int rc = make_plan(num_tokens > 0 ? num_tokens : 1, num_heads, topk, stages_choice(), &pl, tc);
+  if (rc) return rc;
+  *bytes = pl.bytes;
+  return DSA_OK;
+}
+
+int dsa_sparse_attention(const void* q_nope, int64_t q_nope_stride_token, int64_t q_nope_stride_head,
+                         const void* q_pe, int64_t q_pe_stride_token, int64_t q_pe_stride_head,
+                         const void* ckv_cache, int64_t ckv_stride_page, int64_t ckv_stride_row,
+                         const void* kpe_cache, int64_t kpe_stride_page, int64_t kpe_stride_row,
+                         const int32_t* sparse_indices, int64_t indices_stride_token,
+                         int64_t num_tokens, int64_t num_heads, int64_t num_pages, int64_t page_size,
+                         int64_t topk, float sm_scale, void* output, int64_t out_stride_token,
+                         int64_t out_stride_head, float* lse, int64_t lse_stride_token,
+                         int64_t lse_stride_head, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  return attention_impl(q_nope, q_nope_stride_token, q_nope_stride_head, q_pe, q_pe_stride_token,
+                        q_pe_stride_head, ckv_cache, ckv_stride_page, ckv_stride_row, kpe_cache,
+                        kpe_stride_page, kpe_stride_row, sparse_indices, indices_stride_token,
+                        num_tokens, num_heads, num_pages, page_size, topk, sm_scale, output,
+                        out_stride_token, out_stride_head, lse, lse_stride_token, lse_stride_head,
+                        workspace, workspace_bytes, stream, nullptr, nullptr, 0);
+}
+
+int dsa_sparse_attention_scatter(const void* q_nope, int64_t q_nope_stride_token,
+                                 int64_t q_nope_stride_head, const void* q_pe,
+                                 int64_t q_pe_stride_token, int64_t q_pe_stride_head,
+                                 const void* ckv_cache, int64_t ckv_stride_page, int64_t ckv_stride_row,
+                                 const void* kpe_cache, int64_t kpe_stride_page, int64_t kpe_stride_row,
+                                 const int32_t* sparse_indices, int64_t indices_stride_token,
+                                 int64_t num_tokens, int64_t num_heads, int64_t num_pages,
+                                 int64_t page_size, int64_t topk, float sm_scale,
+                                 void* const* out_targets, int64_t out_stride_token,
+                                 int64_t out_stride_head, float* const* lse_targets,
+                                 int64_t lse_stride_token, int64_t lse_stride_head, int num_targets,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+  if (num_targets <= 0 || num_targets > kMaxTargets)
+    return fail(DSA_ERR_INVALID_ARG, "num_targets must be in 1..8");
+  return attention_impl(q_nope, q_nope_stride_token, q_nope_stride_head, q_pe, q_pe_stride_token,
+                        q_pe_stride_head, ckv_cache, ckv_stride_page, ckv_stride_row, kpe_cache,
+                        kpe_stride_page, kpe_stride_row, sparse_indices, indices_stride_token,
+                        num_tokens, num_heads, num_pages, page_size, topk, sm_scale, nullptr,
+                        out_stride_token, out_stride_head, nullptr, lse_stride_token, lse_stride_head,
+                        workspace, workspace_bytes, stream, out_targets, lse_targets, num_targets);
 }
 
 int dsa_read_device_error(const void* workspace, int clear, int* bits, void* stream) {

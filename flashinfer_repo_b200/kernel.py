@@ -107,6 +107,30 @@ def kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, *, outp
         lse = torch.empty((num_tokens, heads), dtype=torch.float32, device=device)
     if num_tokens == 0:
         return output, lse
+    assert output.stride(-1) == 1 and lse.stride(-1) == 1
+
+    _launch("dsa_sparse_attention", q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale,
+            num_tokens, heads, num_pages, topk,
+            (output.data_ptr(), output.stride(0), output.stride(1),
+             lse.data_ptr(), lse.stride(0), lse.stride(1)))
+    return output, lse
+
+
+def _workspace_bytes(device, num_tokens, heads, topk):
+    # the plan (and so the size) also depends on the tuning knobs
+    key = (device.index, num_tokens, heads, topk, os.environ.get("DSA_ATTN_CTAS"),
+           os.environ.get("DSA_ATTN_MIN_TILES"), os.environ.get("DSA_ATTN_STAGES"),
+           os.environ.get("DSA_ATTN_IMPL"))
+    nbytes = _ws_size_cache.get(key)
+    if nbytes is None:
+        n = ctypes.c_size_t(0)
+        _lib.call("dsa_sparse_attention_workspace_size", num_tokens, heads, topk, ctypes.byref(n))
+        nbytes = _ws_size_cache[key] = n.value
+    return nbytes
+
+
+def _launch(fn, q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, num_tokens, heads,
+            num_pages, topk, out_args):
     if sparse_indices.dtype != torch.int32:
         sparse_indices = sparse_indices.to(torch.int32)
     if sparse_indices.stride(-1) != 1:
@@ -115,32 +139,41 @@ def kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, *, outp
     q_pe = _rowmajor(q_pe, 2)
     ckv_cache = _rowmajor(ckv_cache, 8)
     kpe_cache = _rowmajor(kpe_cache, 8)
-    assert output.stride(-1) == 1 and lse.stride(-1) == 1
-
+    device = q_nope.device
     with torch.cuda.device(device):
         stream = torch.cuda.current_stream(device)
-        # the plan (and so the size) also depends on the tuning knobs
-        key = (device.index, num_tokens, heads, topk, os.environ.get("DSA_ATTN_CTAS"),
-               os.environ.get("DSA_ATTN_MIN_TILES"), os.environ.get("DSA_ATTN_STAGES"),
-               os.environ.get("DSA_ATTN_IMPL"))
-        nbytes = _ws_size_cache.get(key)
-        if nbytes is None:
-            n = ctypes.c_size_t(0)
-            _lib.call("dsa_sparse_attention_workspace_size", num_tokens, heads, topk, ctypes.byref(n))
-            nbytes = _ws_size_cache[key] = n.value
+        nbytes = _workspace_bytes(device, num_tokens, heads, topk)
         ws = workspace_for(device).get(device, nbytes, num_tokens * (heads // NUM_HEADS), stream)
         _lib.call(
-            "dsa_sparse_attention",
+            fn,
             q_nope.data_ptr(), q_nope.stride(0), q_nope.stride(1),
             q_pe.data_ptr(), q_pe.stride(0), q_pe.stride(1),
             ckv_cache.data_ptr(), ckv_cache.stride(0), ckv_cache.stride(1),
             kpe_cache.data_ptr(), kpe_cache.stride(0), kpe_cache.stride(1),
             sparse_indices.data_ptr(), sparse_indices.stride(0),
             num_tokens, heads, num_pages, PAGE_SIZE, topk, float(sm_scale),
-            output.data_ptr(), output.stride(0), output.stride(1),
-            lse.data_ptr(), lse.stride(0), lse.stride(1),
-            ws.data_ptr(), ws.numel(), ctypes.c_void_p(stream.cuda_stream))
-    return output, lse
+            *out_args, ws.data_ptr(), ws.numel(), ctypes.c_void_p(stream.cuda_stream))
+
+
+def kernel_scatter(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, out_ptrs,
+                   lse_ptrs, out_strides, lse_strides):
+    """`kernel` whose results are stored into every (out_ptrs[k], lse_ptrs[k])
+    target (device addresses, peer GPUs' included, each offset to where these
+    heads belong; up to 8) with the given (token, head) element strides,
+    instead of into freshly allocated tensors.  Returns nothing; the caller
+    orders the stores (e.g. with a peer barrier)."""
+    num_tokens, heads, num_pages, topk = _check_inputs(q_nope, q_pe, ckv_cache, kpe_cache,
+                                                       sparse_indices)
+    n = len(out_ptrs)
+    assert n == len(lse_ptrs) and 1 <= n <= 8
+    if num_tokens == 0:
+        return
+    outs = (ctypes.c_void_p * n)(*out_ptrs)
+    lses = (ctypes.c_void_p * n)(*lse_ptrs)
+    _launch("dsa_sparse_attention_scatter", q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices,
+            sm_scale, num_tokens, heads, num_pages, topk,
+            (ctypes.cast(outs, ctypes.c_void_p), int(out_strides[0]), int(out_strides[1]),
+             ctypes.cast(lses, ctypes.c_void_p), int(lse_strides[0]), int(lse_strides[1]), n))
 
 
 def kernel_splitk(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, SPLIT_K=None):

@@ -91,6 +91,56 @@ int dsa_sparse_attention(const void* q_nope, int64_t q_nope_stride_token, int64_
                          void* stream);
 
 /*
+ * dsa_sparse_attention_scatter -- dsa_sparse_attention whose epilogues store
+ * the result straight into num_targets (1..8) output/lse buffers instead of
+ * one: out_targets[k] / lse_targets[k] are HOST arrays of device pointers,
+ * each already offset to where this call's heads belong, all with the given
+ * strides.  Replaces the gather step of head-parallel decoding: with the
+ * targets set to every GPU's symmetric output buffer (peer pointers over
+ * NVLink, plain stores, no multicast), each rank computes its head slice and
+ * writes it into every rank's full [T, H_total, 512] output, so the separate
+ * all-gather (and its pack/unpack) disappears.  The caller orders the stores
+ * with its own barrier after the call (the library does not synchronise
+ * ranks).  No counterpart in the reference, whose decode runs on one GPU
+ * (solution/triton/kernel.py:138-182 is the single-GPU operator this splits).
+ */
+int dsa_sparse_attention_scatter(const void* q_nope, int64_t q_nope_stride_token,
+                                 int64_t q_nope_stride_head, const void* q_pe,
+                                 int64_t q_pe_stride_token, int64_t q_pe_stride_head,
+                                 const void* ckv_cache, int64_t ckv_stride_page, int64_t ckv_stride_row,
+                                 const void* kpe_cache, int64_t kpe_stride_page, int64_t kpe_stride_row,
+                                 const int32_t* sparse_indices, int64_t indices_stride_token,
+                                 int64_t num_tokens, int64_t num_heads, int64_t num_pages,
+                                 int64_t page_size, int64_t topk, float sm_scale,
+                                 void* const* out_targets, int64_t out_stride_token,
+                                 int64_t out_stride_head, float* const* lse_targets,
+                                 int64_t lse_stride_token, int64_t lse_stride_head, int num_targets,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Peer buffers and the cross-GPU barrier used with dsa_sparse_attention_scatter
+ * (one process per GPU on one node; no counterpart in the single-GPU reference).
+ *   dsa_peer_alloc  -- cudaMalloc `bytes` (zeroed) and export a CUDA IPC handle
+ *                      (DSA_IPC_HANDLE_BYTES bytes written to ipc_handle);
+ *   dsa_peer_open   -- map another process's buffer from its handle;
+ *   dsa_peer_close / dsa_peer_free -- undo open / alloc;
+ *   dsa_peer_barrier -- one launch on `stream`: rank `rank` of `world` (<= 8)
+ *                      announces its next epoch to every rank and waits until
+ *                      all have announced it.  flags[q] is rank q's flag
+ *                      buffer (>= 9 int32, zeroed, from dsa_peer_alloc) as
+ *                      mapped in this process.  Stores issued before the
+ *                      barrier on the stream are visible to every rank after
+ *                      it.  Waits are bounded (about 2 s); a timeout sets
+ *                      DSA_DEVERR_TIMEOUT in *device_error (if not NULL).
+ */
+#define DSA_IPC_HANDLE_BYTES 64
+int dsa_peer_alloc(size_t bytes, void** ptr, void* ipc_handle);
+int dsa_peer_open(const void* ipc_handle, void** ptr);
+int dsa_peer_close(void* ptr);
+int dsa_peer_free(void* ptr);
+int dsa_peer_barrier(int* const* flags, int rank, int world, int* device_error, void* stream);
+
+/*
  * dsa_sparse_attention_noalloc -- the same operation, arguments and results as
  * dsa_sparse_attention, without the workspace arguments.  This entry point has
  * no counterpart in the reference.  It exists for callers that cannot
