@@ -183,51 +183,62 @@ __device__ __forceinline__ void attn_producer(const AttnParams& p, AttnSmem<NST>
 // ------------------------------------------------------------------ merge
 // LSE merge of the split-K partials (kernel.py:437-493 / the 3-phase merge
 // of :583-704 done in one pass): one CTA per (virtual token, head), launched
-// as a programmatic dependent of the attention grid so that its launch
-// overlaps the attention tail; all SMs merge in parallel.  Thread i owns
-// output columns 4i..4i+3; partials are read 8 at a time.
-__global__ void __launch_bounds__(128) dsa_attention_merge_kernel(const __grid_constant__ AttnParams p) {
+// as a programmatic dependent of the attention grid.  Thread i owns output
+// columns 4i..4i+3.  Partials are taken 8 at a time and every load of a
+// chunk -- each partial's max m, normaliser l and the thread's four columns --
+// is issued before any is used, so a token with at most 8 partials costs one
+// L2 round trip and no barrier; later chunks rescale the running sums
+// (online softmax across chunks).
+constexpr int kMergeThreads = 128;
+constexpr int kMergeChunk = 8;
+
+__global__ void __launch_bounds__(kMergeThreads) dsa_attention_merge_kernel(const __grid_constant__ AttnParams p) {
   asm volatile("griddepcontrol.wait;" ::: "memory");  // attention grid done, writes visible
   const int h = blockIdx.x, v = blockIdx.y, i = threadIdx.x;
   const int tpt = p.tiles_per_token;
   const int c_first = cta_of_tile(p, v * tpt), c_last = cta_of_tile(p, v * tpt + tpt - 1);
   if (c_first == c_last) return;  // written directly by the attention kernel
-  float M = -INFINITY;
-  for (int c0 = c_first; c0 <= c_last; c0 += 8) {  // 8 independent loads per round trip
-    float m[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u)
-      m[u] = (c0 + u <= c_last) ? __ldcg(part_slot(p, c0 + u, v) + kHeads * kDc + h) : -INFINITY;
-#pragma unroll
-    for (int u = 0; u < 8; ++u) M = fmaxf(M, m[u]);
-  }
-  float L = 0.f;
+  // Slot of partial c: every CTA after c_first starts inside this token (its
+  // first segment, slot 0); c_first holds it in slot 1 unless it starts at
+  // the token's first tile.
+  const int first_slot = 2 * c_first + (cta_start(p, c_first) < v * tpt ? 1 : 0);
+  float M = -INFINITY, L = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int c0 = c_first; c0 <= c_last; c0 += 8) {
-    float4 a[8];
-    float w[8];
+  for (int base = c_first; base <= c_last; base += kMergeChunk) {
+    float m[kMergeChunk], l[kMergeChunk];
+    float4 a[kMergeChunk];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      w[u] = 0.f;
+    for (int u = 0; u < kMergeChunk; ++u) {
+      m[u] = -INFINITY;
+      l[u] = 0.f;
       a[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (c0 + u <= c_last) {
-        const float* ps = part_slot(p, c0 + u, v);
-        const float m = __ldcg(ps + kHeads * kDc + h);
-        const float l = __ldcg(ps + kHeads * kDc + kHeads + h);
+      const int c = base + u;
+      if (c <= c_last) {
+        const float* ps = p.part + (int64_t)(c == c_first ? first_slot : 2 * c) * kPartFloats;
+        m[u] = __ldcg(ps + kHeads * kDc + h);
+        l[u] = __ldcg(ps + kHeads * kDc + kHeads + h);
         a[u] = __ldcg(reinterpret_cast<const float4*>(ps + h * kDc) + i);
-        if (m != -INFINITY) {
-          w[u] = exp2f(m - M);
-          L += w[u] * l;
-        }
       }
     }
+    float Mn = M;
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      acc.x += w[u] * a[u].x;
-      acc.y += w[u] * a[u].y;
-      acc.z += w[u] * a[u].z;
-      acc.w += w[u] * a[u].w;
+    for (int u = 0; u < kMergeChunk; ++u) Mn = fmaxf(Mn, m[u]);
+    const float scale = (M == -INFINITY) ? 0.f : exp2f(M - Mn);
+    L *= scale;
+    acc.x *= scale;
+    acc.y *= scale;
+    acc.z *= scale;
+    acc.w *= scale;
+#pragma unroll
+    for (int u = 0; u < kMergeChunk; ++u) {
+      const float w = (m[u] == -INFINITY) ? 0.f : exp2f(m[u] - Mn);
+      L += w * l[u];
+      acc.x += w * a[u].x;
+      acc.y += w * a[u].y;
+      acc.z += w * a[u].z;
+      acc.w += w * a[u].w;
     }
+    M = Mn;
   }
   const int t = v / p.head_groups, grp = v - t * p.head_groups;
   const float inv = (M == -INFINITY) ? 0.f : 1.f / L;
@@ -1125,14 +1136,14 @@ static int attention_impl(const void* q_nope, int64_t q_nope_stride_token, int64
   if (pl.ctas > 1 && stage != 1) {  // tokens split across CTAs: merge grid as a programmatic dependent
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(kHeads, (unsigned)pl.vtokens);
-    cfg.blockDim = dim3(128);
+    cfg.blockDim = dim3(kMergeThreads);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = env_int("DSA_ATTN_PDL", 1) ? 1 : 0;
     e = cudaLaunchKernelEx(&cfg, dsa_attention_merge_kernel, p);
     if (e != cudaSuccess) return fail(DSA_ERR_CUDA, cudaGetErrorString(e));
   }
