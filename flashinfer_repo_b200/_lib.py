@@ -36,9 +36,9 @@ SIGNATURES = {
     "dsa_read_device_error": [P, INT, ctypes.POINTER(INT), P],
     "dsa_indexer_scores": [P, P, I64, P, I64, P, P, I64, P, I64, I64, I64, I64, I64, P, I64, P, P],
     "dsa_index_cache_append": [P, I64, P, P, I64, P, I64, I64, P, P],
-    "dsa_topk_select": [P, I64, P, P, I64, I64, I64, P, P, P],
+    "dsa_topk_select": [P, I64, P, P, I64, I64, I64, P, P, INT, P],
     "dsa_indexer_topk": [P, P, I64, P, I64, P, P, I64, P, I64, I64, I64, I64, I64, I64, P, P, P,
-                         P, P],
+                         INT, P, P],
 }
 
 

@@ -5,18 +5,13 @@
 // it writes every slot equal to the minimum, so ties create duplicates, and
 // it returns logical ids seq_start+pos, :317).  This kernel defines a total
 // order and is exact: for each request the min(k, len) positions with the
-// largest scores, in descending score, ties toward the lower position; the
-// rest of the row is -1.  It also emits the physical slot id
-// block_table[b, pos/64]*64 + pos%64 that the attention operator consumes.
+// largest scores, ties toward the lower position; the rest of the row is -1.
+// Emitted in descending score (order 0) or ascending position (order 1).  It
+// also emits the physical slot id block_table[b, pos/64]*64 + pos%64 that the
+// attention operator consumes.
 //
-// One CTA (1024 threads) per request:
-//  0. rows up to 40960 scores are read once into shared memory;
-//  1. radix select over order-preserving 32-bit keys, digits of 11/11/10
-//     bits, with a shared-memory histogram, finds the k-th largest key T;
-//  2. one pass in index order keeps every key > T and, among keys == T, the
-//     lowest positions (block-wide ballot prefix counts keep index order);
-//  3. a bitonic sort of the (key, ~position) pairs in shared memory.
 #include <cstdio>
+#include <cstdlib>
 
 #include "../../include/dsa_b200.h"
 #include "common.cuh"
@@ -26,7 +21,6 @@ namespace {
 
 constexpr int kTopkThreads = 1024;
 constexpr int kTopkMax = 2048;
-constexpr int kTopkCache = 40960;  // rows up to this length are read from HBM once
 constexpr int kBins = 2048;
 
 // Order-preserving key: larger float -> larger unsigned key; -0.0 and +0.0
@@ -36,18 +30,113 @@ __device__ __forceinline__ uint32_t ordered_key(float x) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// One CTA (1024 threads) per request:
+// 1. The row is read once (float4 loads, 8 in flight per thread), converted to
+//    order-preserving keys and kept in shared memory (rows up to kKeyCache;
+//    longer rows are re-read from L2 in each pass), while the key range
+//    [lo, hi] is reduced.
+// 2. Adaptive radix select: bins span the current range (bin = (key - lo) >>
+//    shift, at most kBins), so even the first pass spreads a real score
+//    distribution; each pass keeps the bin holding the k-th largest key until
+//    the range is one key T (at most three passes; later passes only count
+//    keys inside the range).  Eight histogram copies (one per four warps) cut
+//    atomic contention; the bin is found with one block-wide scan (each thread
+//    sums two bins over the copies).
+// 3. Selection in position order without atomics: warp w owns a contiguous
+//    chunk, lane l four consecutive keys per round.  A counting pass (plain
+//    per-thread sums) gives per-warp counts of keys > T and == T; one scan over
+//    the 32 warps gives each warp its output offset and its share of the
+//    wanted equal keys (ties go to the lowest positions); a writing pass
+//    places (key << 32 | ~position) words with one warp scan per round.
+// 4. Order 0 only: a bitonic sort of those words, descending (score, then
+//    lower position): strides below 64 in registers with warp shuffles,
+//    larger ones in shared memory.
+constexpr int kHistCopies = 8;
+constexpr int kKeyCache = 32768;
+
 struct TopkSmem {
   unsigned long long buf[kTopkMax];
-  uint32_t hist[kBins];
-  uint32_t warp_cnt[kTopkThreads / 32];
-  uint32_t digit, above;
-  float cache[kTopkCache];
+  uint32_t hist[kHistCopies][kBins];
+  uint32_t red_lo[32], red_hi[32];
+  uint32_t w_cnt[32], w_off[32], w_eqb[32];
+  uint32_t lo, hi, bstar, above;
+  uint4 keys[kKeyCache / 4];
 };
+
+__device__ __forceinline__ unsigned long long shfl_xor64(unsigned long long v, int m) {
+  const uint32_t lo = __shfl_xor_sync(0xffffffffu, (uint32_t)v, m);
+  const uint32_t hi = __shfl_xor_sync(0xffffffffu, (uint32_t)(v >> 32), m);
+  return ((unsigned long long)hi << 32) | lo;
+}
+
+// Descending bitonic sort of buf[0, P), P a power of two in [64, 2048];
+// 1024 threads, warp w holds words 64w + lane and 64w + 32 + lane.
+__device__ void bitonic_desc(unsigned long long* buf, int P, int warp, int lane) {
+  const bool active = warp * 64 < P;
+  unsigned long long v0 = 0, v1 = 0;
+  const int e0 = warp * 64 + lane, e1 = e0 + 32;
+  if (active) {
+    v0 = buf[e0];
+    v1 = buf[e1];
+  }
+  for (int size = 2; size <= P; size <<= 1) {
+    if (size > 64) {
+      if (active) {
+        buf[e0] = v0;
+        buf[e1] = v1;
+      }
+      __syncthreads();
+      for (int st = size >> 1; st >= 64; st >>= 1) {
+        for (int i = warp * 32 + lane; i < P / 2; i += kTopkThreads) {
+          const int l = 2 * i - (i & (st - 1));
+          const int h = l + st;
+          const bool desc = (l & size) == 0;
+          const unsigned long long a = buf[l], c = buf[h];
+          if ((a < c) == desc) {
+            buf[l] = c;
+            buf[h] = a;
+          }
+        }
+        __syncthreads();
+      }
+      if (active) {
+        v0 = buf[e0];
+        v1 = buf[e1];
+      }
+    }
+    for (int st = min(size >> 1, 32); st >= 1; st >>= 1) {
+      if (st == 32) {
+        const bool desc = (e0 & size) == 0;
+        if ((v0 < v1) == desc) {
+          const unsigned long long t = v0;
+          v0 = v1;
+          v1 = t;
+        }
+      } else {
+        const bool low = (lane & st) == 0;
+        const unsigned long long p0 = shfl_xor64(v0, st), p1 = shfl_xor64(v1, st);
+        const bool d0 = (e0 & size) == 0, d1 = (e1 & size) == 0;
+        // the low element of a pair keeps the larger word when descending
+        v0 = (low == d0) ? (v0 > p0 ? v0 : p0) : (v0 < p0 ? v0 : p0);
+        v1 = (low == d1) ? (v1 > p1 ? v1 : p1) : (v1 < p1 ? v1 : p1);
+      }
+    }
+  }
+  if (active) {
+    buf[e0] = v0;
+    buf[e1] = v1;
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ uint4 keys4(const float4 v) {
+  return make_uint4(ordered_key(v.x), ordered_key(v.y), ordered_key(v.z), ordered_key(v.w));
+}
 
 __global__ void __launch_bounds__(kTopkThreads)
     dsa_topk_kernel(const float* __restrict__ scores, int64_t stride, const int32_t* seq_lens,
-                    const int32_t* block_table, int64_t bt_stride, int k, int32_t* positions,
-                    int32_t* slots) {
+                     const int32_t* block_table, int64_t bt_stride, int k, int32_t* positions,
+                     int32_t* slots, int order) {
   extern __shared__ __align__(16) uint8_t topk_smem[];
   TopkSmem& S = *reinterpret_cast<TopkSmem*>(topk_smem);
   const int b = blockIdx.x;
@@ -55,148 +144,254 @@ __global__ void __launch_bounds__(kTopkThreads)
   const int len = max(0, seq_lens[b]);
   const float* sc = scores + (int64_t)b * stride;
   const int n_out = min(k, len);
-  const bool cached = len <= kTopkCache;
+  // shared-memory keys need 16-byte aligned rows for the vector loads
+  const bool cached = len <= kKeyCache && ((reinterpret_cast<uintptr_t>(sc) & 15) == 0);
+  const int n4 = (len + 3) >> 2;  // groups of four keys
 
-  for (int i = tid; i < kTopkMax; i += kTopkThreads) S.buf[i] = 0ull;  // sorts last
-  if (cached) {  // one pass over HBM/L2, 8 loads in flight per thread
-    for (int base = 0; base < len; base += 8 * kTopkThreads) {
-      float v[8];
+  // key group g (positions 4g..4g+3; positions >= len read as key 0, never taken)
+  auto group_at = [&](int g) -> uint4 {
+    if (cached) return S.keys[g];
+    uint4 r;
+    const int i = 4 * g;
+    r.x = i < len ? ordered_key(__ldcg(sc + i)) : 0u;
+    r.y = i + 1 < len ? ordered_key(__ldcg(sc + i + 1)) : 0u;
+    r.z = i + 2 < len ? ordered_key(__ldcg(sc + i + 2)) : 0u;
+    r.w = i + 3 < len ? ordered_key(__ldcg(sc + i + 3)) : 0u;
+    return r;
+  };
+
+  // ---- 1. load and key range
+  uint32_t tlo = 0xffffffffu, thi = 0u;
+  auto fold = [&](uint32_t key, int i) {
+    if (i < len) {
+      tlo = min(tlo, key);
+      thi = max(thi, key);
+    }
+  };
+  if (cached) {
+    const float4* s4 = reinterpret_cast<const float4*>(sc);
+    for (int base = 0; base < n4; base += 8 * kTopkThreads) {
+      float4 v[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int i = base + j * kTopkThreads + tid;
-        v[j] = i < len ? __ldcs(sc + i) : 0.f;
+        const int g = base + j * kTopkThreads + tid;
+        v[j] = g < n4 ? __ldcs(s4 + g) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int i = base + j * kTopkThreads + tid;
-        if (i < len) S.cache[i] = v[j];
+        const int g = base + j * kTopkThreads + tid;
+        if (g < n4) {
+          uint4 kk = keys4(v[j]);
+          const int i = 4 * g;
+          if (i + 1 >= len) kk.y = 0u;  // a partial last group: keys past len are 0
+          if (i + 2 >= len) kk.z = 0u;
+          if (i + 3 >= len) kk.w = 0u;
+          S.keys[g] = kk;
+          fold(kk.x, i);
+          fold(kk.y, i + 1);
+          fold(kk.z, i + 2);
+          fold(kk.w, i + 3);
+        }
       }
     }
-    __syncthreads();
+  } else {
+    for (int g = tid; g < n4; g += kTopkThreads) {
+      const uint4 kk = group_at(g);
+      fold(kk.x, 4 * g);
+      fold(kk.y, 4 * g + 1);
+      fold(kk.z, 4 * g + 2);
+      fold(kk.w, 4 * g + 3);
+    }
   }
-  auto score_at = [&](int i) -> float { return cached ? S.cache[i] : __ldcg(sc + i); };
+  tlo = __reduce_min_sync(0xffffffffu, tlo);
+  thi = __reduce_max_sync(0xffffffffu, thi);
+  if (lane == 0) {
+    S.red_lo[warp] = tlo;
+    S.red_hi[warp] = thi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t a = __reduce_min_sync(0xffffffffu, S.red_lo[lane]);
+    const uint32_t c = __reduce_max_sync(0xffffffffu, S.red_hi[lane]);
+    if (lane == 0) {
+      S.lo = a;
+      S.hi = c;
+    }
+  }
+  __syncthreads();
 
-  uint32_t prefix = 0, mask = 0;
-  int need = n_out;  // elements still to take from the class equal to the threshold
-  if (len > k) {
-    // digits of 11, 11 and 10 bits, most significant first
-    for (int pass = 0; pass < 3; ++pass) {
-      const int shift = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
-      const int bits = pass == 2 ? 10 : 11;
-      const uint32_t dmask = (1u << bits) - 1u;
-      for (int i = tid; i < kBins; i += kTopkThreads) S.hist[i] = 0;
+  // ---- 2. exact threshold key T and how many keys == T are wanted
+  uint32_t lo = S.lo, hi = S.hi;
+  int need = n_out;
+  const bool all = len <= k;
+  if (!all) {
+    uint32_t* hist0 = &S.hist[0][0];
+    uint32_t* mine = S.hist[warp & (kHistCopies - 1)];
+    while (lo != hi) {
+      const uint32_t range = hi - lo;
+      int shift = 0;
+      while ((range >> shift) >= (uint32_t)kBins) ++shift;
+      const int nb = (int)(range >> shift) + 1;
+      for (int j = tid; j < kHistCopies * kBins; j += kTopkThreads) hist0[j] = 0;
       __syncthreads();
-      for (int base = 0; base < len; base += kTopkThreads) {
-        const int i = base + tid;
-        uint32_t key = 0;
-        bool in = false;
-        if (i < len) {
-          key = ordered_key(score_at(i));
-          in = (key & mask) == prefix;
-        }
-        // warp-aggregated increment: real score distributions pile into a few
-        // bins, and per-thread shared atomics on one address serialise
-        const unsigned active = __ballot_sync(0xffffffffu, in);
-        if (in) {
-          const uint32_t bin = (key >> shift) & dmask;
-          const unsigned peers = __match_any_sync(active, bin);
-          if ((__ffs(peers) - 1) == lane) atomicAdd(&S.hist[bin], (uint32_t)__popc(peers));
-        }
+      for (int g = tid; g < n4; g += kTopkThreads) {
+        const uint4 kk = group_at(g);
+        const int i = 4 * g;
+        if (kk.x >= lo && kk.x <= hi) atomicAdd(&mine[(kk.x - lo) >> shift], 1u);
+        if (i + 1 < len && kk.y >= lo && kk.y <= hi) atomicAdd(&mine[(kk.y - lo) >> shift], 1u);
+        if (i + 2 < len && kk.z >= lo && kk.z <= hi) atomicAdd(&mine[(kk.z - lo) >> shift], 1u);
+        if (i + 3 < len && kk.w >= lo && kk.w <= hi) atomicAdd(&mine[(kk.w - lo) >> shift], 1u);
       }
       __syncthreads();
-      if (warp == 0) {
-        // digit d with count(> d) < need <= count(>= d): bins scanned from the
-        // top, 64 per lane, warp prefix sum over the lanes
-        const int nb = 1 << bits, per = nb / 32;
-        uint32_t tot = 0;
-        for (int j = 0; j < per; ++j) tot += S.hist[nb - 1 - (lane * per + j)];
-        uint32_t incl = tot;
+      {
+        // bin b* (from the top) with count(above) < need <= count(above) + count(b*):
+        // thread t holds bins kBins-1-2t and kBins-2-2t (zero past nb), then a
+        // block-wide exclusive scan in top-down order
+        const int d_hi = kBins - 1 - 2 * tid, d_lo = d_hi - 1;
+        uint32_t a = 0, c = 0;
+#pragma unroll
+        for (int q = 0; q < kHistCopies; ++q) {
+          a += S.hist[q][d_hi];
+          c += S.hist[q][d_lo];
+        }
+        if (d_hi >= nb) a = 0;
+        if (d_lo >= nb) c = 0;
+        const uint32_t sum = a + c;
+        uint32_t incl = sum;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
           const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
           if (lane >= o) incl += y;
         }
-        uint32_t run = incl - tot;
-        if (run < (uint32_t)need && incl >= (uint32_t)need) {
-          for (int j = 0; j < per; ++j) {
-            const int d = nb - 1 - (lane * per + j);
-            const uint32_t h = S.hist[d];
-            if (run < (uint32_t)need && run + h >= (uint32_t)need) {
-              S.digit = d;
-              S.above = run;
-            }
-            run += h;
-          }
+        if (lane == 31) S.w_cnt[warp] = incl;
+        __syncthreads();
+        uint32_t wsum = lane < warp ? S.w_cnt[lane] : 0u;
+        wsum = __reduce_add_sync(0xffffffffu, wsum);
+        const uint32_t run = wsum + incl - sum;  // keys in bins above d_hi
+        if (run < (uint32_t)need && run + a >= (uint32_t)need) {
+          S.bstar = (uint32_t)d_hi;
+          S.above = run;
+        } else if (run + a < (uint32_t)need && run + sum >= (uint32_t)need) {
+          S.bstar = (uint32_t)d_lo;
+          S.above = run + a;
         }
       }
       __syncthreads();
+      const uint32_t d = S.bstar;
       need -= (int)S.above;
-      prefix |= S.digit << shift;
-      mask |= dmask << shift;
-      __syncthreads();
+      const uint32_t nlo = lo + (d << shift);
+      hi = (uint32_t)min((unsigned long long)hi, (unsigned long long)nlo + (1ull << shift) - 1ull);
+      lo = nlo;
+      __syncthreads();  // S.bstar / S.above / the histograms are rewritten by the next pass
     }
   }
-  // Threshold key T = prefix (all keys qualify when len <= k).  Keep keys > T
-  // and the first `need` keys == T in position order.
-  const uint32_t T = prefix;
-  const bool all = len <= k;
-  int taken_gt = 0, taken_eq = 0;
-  const int n_gt = n_out - need;  // slots [0, n_gt) for keys > T, then equal keys
-  for (int base = 0; base < len; base += kTopkThreads) {
-    const int i = base + tid;
-    uint32_t key = 0;
-    bool gt = false, eq = false;
-    if (i < len) {
-      key = ordered_key(score_at(i));
-      gt = all || key > T;
-      eq = !all && key == T;
+  const uint32_t T = lo;  // with `all`, every key is taken
+
+  // ---- 3. selection in position order
+  // warp w owns groups [w*cg, (w+1)*cg), lane l takes group w*cg + r*32 + l in round r
+  const int cg = (((n4 + 31) / 32) + 31) / 32 * 32;
+  const int g0 = warp * cg, g1 = min(n4, g0 + cg);
+  auto flags = [&](const uint4& kk, int i, uint32_t& gt, uint32_t& eq) {
+    const uint32_t v[4] = {kk.x, kk.y, kk.z, kk.w};
+    gt = 0;
+    eq = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const bool in = i + q < len;
+      gt |= (uint32_t)(in && (all || v[q] > T)) << q;
+      eq |= (uint32_t)(in && !all && v[q] == T) << q;
     }
-    const uint32_t bg = __ballot_sync(0xffffffffu, gt), be = __ballot_sync(0xffffffffu, eq);
-    if (lane == 0) S.warp_cnt[warp] = (__popc(bg) << 16) | __popc(be);
-    __syncthreads();
-    // exclusive prefix of the per-warp counts (both packed in one word)
-    const uint32_t cnt = S.warp_cnt[lane];
-    uint32_t incl = cnt;
+  };
+  uint32_t n_gt = 0, n_eq = 0;
+  for (int g = g0 + lane; g < g1; g += 32) {
+    uint32_t gt, eq;
+    flags(group_at(g), 4 * g, gt, eq);
+    n_gt += __popc(gt);
+    n_eq += __popc(eq);
+  }
+  const uint32_t packed = __reduce_add_sync(0xffffffffu, (n_gt << 16) | n_eq);
+  if (lane == 0) S.w_cnt[warp] = packed;
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t pk = S.w_cnt[lane];
+    const uint32_t g = pk >> 16, e = pk & 0xffffu;
+    uint32_t eb = e;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += y;
+      const uint32_t y = __shfl_up_sync(0xffffffffu, eb, o);
+      if (lane >= o) eb += y;
     }
-    const uint32_t excl = __shfl_sync(0xffffffffu, incl - cnt, warp);
-    const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
-    const uint32_t off_g = excl >> 16, off_e = excl & 0xffffu;
-    const uint32_t tot_g = total >> 16, tot_e = total & 0xffffu;
-    const uint32_t lt = (1u << lane) - 1u;
-    const unsigned long long comp =
-        ((unsigned long long)key << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)i);
-    if (gt) {
-      const int slot = taken_gt + (int)(off_g + __popc(bg & lt));
-      if (slot < kTopkMax) S.buf[slot] = comp;
+    eb -= e;  // equal keys in earlier warps
+    const uint32_t want = (uint32_t)need > eb ? min(e, (uint32_t)need - eb) : 0u;
+    const uint32_t cnt = g + want;
+    uint32_t off = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, off, o);
+      if (lane >= o) off += y;
     }
-    if (eq) {
-      const int r = taken_eq + (int)(off_e + __popc(be & lt));
-      if (r < need) S.buf[n_gt + r] = comp;
-    }
-    taken_gt += (int)tot_g;
-    taken_eq += (int)tot_e;
-    __syncthreads();
+    S.w_off[lane] = off - cnt;
+    S.w_eqb[lane] = eb;
   }
-  // Bitonic sort, descending, over kTopkMax entries.
-  for (int size = 2; size <= kTopkMax; size <<= 1) {
-    for (int stride2 = size >> 1; stride2 > 0; stride2 >>= 1) {
-      for (int i = tid; i < kTopkMax / 2; i += kTopkThreads) {
-        const int lo = 2 * i - (i & (stride2 - 1));
-        const int hi = lo + stride2;
-        const bool desc = ((lo & size) == 0);
-        const unsigned long long a = S.buf[lo], c = S.buf[hi];
-        if ((a < c) == desc) {
-          S.buf[lo] = c;
-          S.buf[hi] = a;
-        }
+  __syncthreads();
+  {
+    uint32_t off = S.w_off[warp], eq_rank = S.w_eqb[warp];
+    for (int gr = g0; gr < g1; gr += 32) {
+      const int g = gr + lane;
+      uint4 kk = make_uint4(0u, 0u, 0u, 0u);
+      uint32_t gt = 0, eq = 0;
+      if (g < g1) {
+        kk = group_at(g);
+        flags(kk, 4 * g, gt, eq);
       }
-      __syncthreads();
+      // one lane-exclusive scan of (keys > T, keys == T) packed 16|16, in position order
+      const uint32_t ng = __popc(gt), ne = __popc(eq);
+      uint32_t pk = (ng << 16) | ne;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, pk, o);
+        if (lane >= o) pk += y;
+      }
+      const uint32_t tot = __shfl_sync(0xffffffffu, pk, 31);
+      pk -= (ng << 16) | ne;
+      const uint32_t pg = pk >> 16, pe = pk & 0xffffu;
+      // equal keys are wanted while their rank (position order) is below need
+      const uint32_t room = (uint32_t)need > eq_rank ? (uint32_t)need - eq_rank : 0u;
+      const uint32_t eq_before = min(pe, room);  // wanted equal keys in earlier lanes
+      uint32_t take = gt;
+      {
+        uint32_t r = pe;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if ((eq >> q) & 1u) {
+            if (r < room) take |= 1u << q;
+            ++r;
+          }
+      }
+      const uint32_t pt = pg + eq_before;
+      const uint32_t tot_t = (tot >> 16) + min(tot & 0xffffu, room);
+      const uint32_t tot_e = tot & 0xffffu;
+      const uint32_t v[4] = {kk.x, kk.y, kk.z, kk.w};
+      uint32_t w = off + pt;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if ((take >> q) & 1u) {
+          if (w < (uint32_t)kTopkMax)
+            S.buf[w] = ((unsigned long long)v[q] << 32) | (0xFFFFFFFFu - (uint32_t)(4 * g + q));
+          ++w;
+        }
+      off += tot_t;
+      eq_rank += tot_e;
     }
   }
+  int P = 64;
+  while (P < n_out) P <<= 1;
+  __syncthreads();
+  for (int j = n_out + tid; j < P; j += kTopkThreads) S.buf[j] = 0ull;  // sorts last
+  __syncthreads();
+
+  // ---- 4. order by score (order 0); order 1 keeps position order
+  if (order == 0) bitonic_desc(S.buf, P, warp, lane);
   for (int j = tid; j < k; j += kTopkThreads) {
     int32_t pos = -1, slot = -1;
     if (j < n_out) {
@@ -215,9 +410,11 @@ using namespace dsa;
 
 extern "C" int dsa_topk_select(const float* scores, int64_t scores_stride, const int32_t* seq_lens,
                                const int32_t* block_table, int64_t block_table_stride, int64_t batch,
-                               int64_t k, int32_t* positions, int32_t* slots, void* stream) {
+                               int64_t k, int32_t* positions, int32_t* slots, int order,
+                               void* stream) {
   if (batch < 0) return report_error(DSA_ERR_INVALID_ARG, "negative batch");
   if (k <= 0 || k > kTopkMax) return report_error(DSA_ERR_UNSUPPORTED, "k must be in [1, 2048]");
+  if (order != 0 && order != 1) return report_error(DSA_ERR_INVALID_ARG, "order must be 0 or 1");
   if (batch == 0) return DSA_OK;
   if (!scores || !seq_lens || !positions || (slots && !block_table))
     return report_error(DSA_ERR_INVALID_ARG, "NULL pointer argument");
@@ -225,7 +422,8 @@ extern "C" int dsa_topk_select(const float* scores, int64_t scores_stride, const
   cudaError_t e = cudaFuncSetAttribute(dsa_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return report_error(DSA_ERR_CUDA, cudaGetErrorString(e));
   dsa_topk_kernel<<<(unsigned)batch, kTopkThreads, smem, static_cast<cudaStream_t>(stream)>>>(
-      scores, scores_stride, seq_lens, block_table, block_table_stride, (int)k, positions, slots);
+      scores, scores_stride, seq_lens, block_table, block_table_stride, (int)k, positions, slots,
+      order);
   e = cudaGetLastError();
   if (e != cudaSuccess) return report_error(DSA_ERR_CUDA, cudaGetErrorString(e));
   return DSA_OK;
@@ -237,12 +435,12 @@ extern "C" int dsa_indexer_topk(const void* q_fp8, const void* k_cache_fp8, int6
                                 const int32_t* seq_lens, int64_t batch, int64_t num_heads,
                                 int64_t head_dim, int64_t num_pages, int64_t max_len, int64_t k,
                                 float* scores_workspace, int32_t* positions, int32_t* slots,
-                                int* device_error, void* stream) {
+                                int order, int* device_error, void* stream) {
   int rc = dsa_indexer_scores(q_fp8, k_cache_fp8, k_page_stride, k_scale, scale_page_stride,
                               weights, block_table, block_table_stride, seq_lens, batch, num_heads,
                               head_dim, num_pages, max_len, scores_workspace, max_len, device_error,
                               stream);
   if (rc != DSA_OK) return rc;
   return dsa_topk_select(scores_workspace, max_len, seq_lens, block_table, block_table_stride, batch,
-                         k, positions, slots, stream);
+                         k, positions, slots, order, stream);
 }

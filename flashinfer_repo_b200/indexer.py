@@ -83,10 +83,13 @@ def indexer_scores(q_fp8, k_cache_fp8, k_scale, weights, seq_lens, block_table, 
     return out
 
 
-def topk_select(scores, seq_lens, block_table=None, topk=2048):
-    """Exact top-k per row of `scores` [B, L] over the first seq_lens[b] entries.
-    Returns (positions [B, topk] int32, slots [B, topk] int32 or None), -1 padded,
-    descending score, ties toward the lower position."""
+def topk_select(scores, seq_lens, block_table=None, topk=2048, order="score"):
+    """Exact top-k per row of `scores` [B, L] over the first seq_lens[b] entries
+    (ties toward the lower position).  Returns (positions [B, topk] int32,
+    slots [B, topk] int32 or None), -1 padded; order "score" emits descending
+    score (ties by ascending position), "position" emits ascending position
+    (skips the sort)."""
+    assert order in ("score", "position")
     assert scores.dtype == torch.float32 and scores.stride(-1) == 1 and scores.is_cuda
     B = scores.shape[0]
     seq_lens = seq_lens.to(torch.int32).contiguous()
@@ -101,16 +104,18 @@ def topk_select(scores, seq_lens, block_table=None, topk=2048):
         stream = torch.cuda.current_stream(scores.device).cuda_stream
         _lib.call("dsa_topk_select", scores.data_ptr(), scores.stride(0), seq_lens.data_ptr(), bt_ptr,
                   bt_stride, B, int(topk), pos.data_ptr(),
-                  slots.data_ptr() if slots is not None else None, ctypes.c_void_p(stream))
+                  slots.data_ptr() if slots is not None else None, 0 if order == "score" else 1,
+                  ctypes.c_void_p(stream))
     return pos, slots
 
 
-def indexer_topk(q_fp8, k_cache_fp8, k_scale, weights, seq_lens, block_table, topk=2048, **kw):
+def indexer_topk(q_fp8, k_cache_fp8, k_scale, weights, seq_lens, block_table, topk=2048,
+                 order="score", **kw):
     """Indexer scores then exact top-k; returns (positions, slots).  `slots`
     can be passed straight to `kernel()` as `sparse_indices` (one row per
     request / decode token)."""
     scores = indexer_scores(q_fp8, k_cache_fp8, k_scale, weights, seq_lens, block_table, **kw)
-    return topk_select(scores, seq_lens, block_table, topk)
+    return topk_select(scores, seq_lens, block_table, topk, order)
 
 
 def index_cache_append(keys, slot_ids, k_cache_fp8, k_scale, *, num_pages=None, k_page_stride=None,

@@ -26,10 +26,11 @@ def run_sparse_attention_pipeline(q_index_fp8, k_index_cache_fp8, k_scale, weigh
                                   lse=None):
     """One DSA step.  Index tensors are per request ([B,...]); q_nope/q_pe are
     per query token ([T,16k,*]).  Returns (output [T,H,512] bf16, lse [T,H]
-    fp32 base 2, slots [B,topk] int32)."""
+    fp32 base 2, slots [B,topk] int32 in ascending token position)."""
     scores = IX.indexer_scores(q_index_fp8, k_index_cache_fp8, k_scale, weights, seq_lens,
                                block_table, out=scores_out)
-    _, slots = IX.topk_select(scores, seq_lens, block_table, topk)
+    # position order: the attention operator does not need score order
+    _, slots = IX.topk_select(scores, seq_lens, block_table, topk, order="position")
     sparse_indices = slots if query_request is None else slots.index_select(0, query_request)
     out, lse = kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, output=output,
                       lse=lse)

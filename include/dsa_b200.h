@@ -194,15 +194,18 @@ int dsa_indexer_scores(const void* q_fp8, const void* k_cache_fp8, int64_t k_pag
 /*
  * Exact top-k of each request's scores.  Replaces topk_kernel
  * (solution/triton/indexer_kernel.py:289-343, launched at :422-431): the
- * min(k, seq_lens[b]) positions with the largest scores, in descending score,
- * ties toward the lower position, then -1.  positions[b, j] is the token
- * position inside the request; slots[b, j] (optional, NULL to skip) is the
- * flat physical slot block_table[b, pos/64]*64 + pos%64 that
+ * min(k, seq_lens[b]) positions with the largest scores (ties toward the
+ * lower position), then -1.  order 0: emitted in descending score, ties by
+ * ascending position; order 1: emitted in ascending position (no sort; the
+ * attention operator does not depend on the order, and the reference's
+ * replace-the-minimum loop leaves it unspecified).  positions[b, j] is the
+ * token position inside the request; slots[b, j] (optional, NULL to skip) is
+ * the flat physical slot block_table[b, pos/64]*64 + pos%64 that
  * dsa_sparse_attention consumes.  1 <= k <= 2048.
  */
 int dsa_topk_select(const float* scores, int64_t scores_stride, const int32_t* seq_lens,
                     const int32_t* block_table, int64_t block_table_stride, int64_t batch, int64_t k,
-                    int32_t* positions, int32_t* slots, void* stream);
+                    int32_t* positions, int32_t* slots, int order, void* stream);
 
 /*
  * Indexer scores followed by top-k (replaces run_indexer_and_topk,
@@ -214,7 +217,7 @@ int dsa_indexer_topk(const void* q_fp8, const void* k_cache_fp8, int64_t k_page_
                      const int32_t* block_table, int64_t block_table_stride, const int32_t* seq_lens,
                      int64_t batch, int64_t num_heads, int64_t head_dim, int64_t num_pages,
                      int64_t max_len, int64_t k, float* scores_workspace, int32_t* positions,
-                     int32_t* slots, int* device_error, void* stream);
+                     int32_t* slots, int order, int* device_error, void* stream);
 
 /*
  * Quantise new index keys and append them to the paged FP8 index-key cache

@@ -98,9 +98,10 @@ def indexer_scores(q, k_cache, k_page_stride, scale_base, s_page_stride, w, bloc
     return out
 
 
-def topk(scores, seq_lens, block_table, k, nthreads=None):
-    """Exact top-k (descending score, ties -> lower position).  Returns
-    (positions int32 [B,k], slots int32 [B,k]), -1 padded."""
+def topk(scores, seq_lens, block_table, k, nthreads=None, order="score"):
+    """Exact top-k (ties -> lower position).  Returns (positions int32 [B,k],
+    slots int32 [B,k]), -1 padded; order "score": descending score, ties by
+    ascending position; "position": the same set in ascending position."""
     scores = np.ascontiguousarray(scores, dtype=np.float32)
     sl = np.ascontiguousarray(seq_lens, dtype=np.int32)
     bt = np.ascontiguousarray(block_table, dtype=np.int32)
@@ -109,6 +110,12 @@ def topk(scores, seq_lens, block_table, k, nthreads=None):
     slots = np.empty((B, k), np.int32)
     lib().oracle_topk(_p(scores), B, L, _p(sl), _p(bt), bt.shape[1], int(k), _p(pos), _p(slots),
                       _threads(nthreads))
+    if order == "position":
+        for b in range(B):
+            n = int((pos[b] >= 0).sum())
+            perm = np.argsort(pos[b, :n], kind="stable")
+            pos[b, :n] = pos[b, :n][perm]
+            slots[b, :n] = slots[b, :n][perm]
     return pos, slots
 
 

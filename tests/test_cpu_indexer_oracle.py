@@ -46,6 +46,9 @@ def test_topk_order_and_ties():
     assert slots.tolist() == [[7 * 64 + 1, 7 * 64 + 2, 7 * 64 + 4, 7 * 64 + 3, 7 * 64 + 7]]
     pos, _ = O.topk(scores, np.array([3], np.int32), bt, 5)
     assert pos.tolist() == [[1, 2, 0, -1, -1]]
+    pos, slots = O.topk(scores, np.array([8], np.int32), bt, 5, order="position")
+    assert pos.tolist() == [[1, 2, 3, 4, 7]]
+    assert slots.tolist() == [[7 * 64 + 1, 7 * 64 + 2, 7 * 64 + 3, 7 * 64 + 4, 7 * 64 + 7]]
 
 
 def test_e4m3_exact_generator_values():

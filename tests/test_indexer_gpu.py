@@ -111,3 +111,25 @@ def test_topk_long_and_tied_rows(cuda_device, L):
     rpos, rslots = O.topk(scores, lens, bt, 2048)
     assert np.array_equal(pos.cpu().numpy(), rpos) and np.array_equal(slots.cpu().numpy(), rslots)
     assert rpos[1].tolist() == list(range(2048))
+
+
+@pytest.mark.parametrize("L", [32768, 40961, 3000])
+def test_topk_position_order(cuda_device, L):
+    """order="position" returns the same set as the score order, in ascending
+    position (tie-heavy rows and an all-equal row included)."""
+    rng = np.random.default_rng(L + 7)
+    B = 3
+    scores = rng.standard_normal((B, L)).astype(np.float32)
+    scores[1] = np.round(scores[1] * 2) / 2  # heavy ties
+    scores[2] = 0.5                           # all equal
+    lens = np.array([L, L - 5, L], np.int32)
+    bt = rng.permutation(B * ((L + 63) // 64)).astype(np.int32).reshape(B, -1)
+
+    def dev(a):
+        return torch.from_numpy(a).to(cuda_device)
+    pos, slots = IX.topk_select(dev(scores), dev(lens), dev(bt), 2048, order="position")
+    rpos, rslots = O.topk(scores, lens, bt, 2048, order="position")
+    assert np.array_equal(pos.cpu().numpy(), rpos) and np.array_equal(slots.cpu().numpy(), rslots)
+    spos, _ = IX.topk_select(dev(scores), dev(lens), dev(bt), 2048)
+    for b in range(B):
+        assert sorted(spos[b].cpu().tolist()) == sorted(rpos[b].tolist())

@@ -32,7 +32,7 @@ def _setup(dev, seq_lens, tokens_per_request=1):
 def _oracle(ic, host, query_request):
     max_len = ic.block_table.shape[1] * 64
     scores = oracle_indexer(ic, max_len)
-    _, slots = O.topk(scores, ic.seq_lens, ic.block_table, 2048)
+    _, slots = O.topk(scores, ic.seq_lens, ic.block_table, 2048, order="position")
     qn, qp, ckv, kpe = host
     out, lse = O.dsa_attention(qn, qp, ckv, kpe, slots[query_request], W.SM_SCALE)
     return slots, out, lse
