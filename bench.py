@@ -64,6 +64,34 @@ class L2Flush:
         torch.sum(self.r, dim=0, out=self.acc)
 
 
+def graph_timed_steps(fn, steps, flush, side, stream, per_graph=50):
+    """Device time (ms) of each of `steps` calls of fn(), run as CUDA-graph
+    nodes: every captured step is flush(), a start event, fn(), an end event
+    (events recorded as graph nodes); the graph holds min(per_graph, steps)
+    steps and is replayed until `steps` have run."""
+    n = min(per_graph, steps)
+    starts = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(n)]
+    ends = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(n)]
+    side.wait_stream(stream)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        fn()  # first-call set-up outside the capture
+        with torch.cuda.graph(g, stream=side):
+            for j in range(n):
+                flush(j)
+                starts[j].record(side)
+                fn()
+                ends[j].record(side)
+    stream.wait_stream(side)
+    torch.cuda.synchronize()
+    times = []
+    while len(times) < steps:
+        g.replay()
+        torch.cuda.synchronize()
+        times += [starts[j].elapsed_time(ends[j]) for j in range(min(n, steps - len(times)))]
+    return times
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -223,140 +251,142 @@ def run_ours(args):
     if read_device_error(dev):
         raise SystemExit("device error flag set during warm-up")
 
-    # ---- device-resident timing (value + roofline): the operator call is
-    # captured once in a CUDA graph (attention grid + merge grid) and replayed
-    # per step, so the step time is device time, not Python launch latency
-    graph = torch.cuda.CUDAGraph()
+    # ---- device-resident timing (value + roofline).  Steps run as CUDA-graph
+    # nodes: each captured step is the untimed L2 flush, a start event, the
+    # operator call (attention grid + merge grid), an end event; one graph
+    # holds up to 50 steps and is replayed until K steps have run.  A step's
+    # time is its event interval on the device, so neither Python nor a graph
+    # launch per step is counted, as inside a decode step captured whole.
     side = torch.cuda.Stream(dev)
-    side.wait_stream(stream)
-    with torch.cuda.stream(side):
-        with torch.cuda.graph(graph, stream=side):
-            kernel(qn, qp, ckv, kpe, idx, scale, output=out, lse=lse)
-    stream.wait_stream(side)
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+
+    def op():
+        kernel(qn, qp, ckv, kpe, idx, scale, output=out, lse=lse)
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
-        for i in range(args.steps):
-            flush(i)
-            starts[i].record(stream)
-            graph.replay()
-            ends[i].record(stream)
-        torch.cuda.synchronize()
+        step_ms = graph_timed_steps(op, args.steps, flush, side, stream)
         if dist:
             dist.barrier()
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_ms = sum(step_ms)
     clocks = clk.summary()
 
     # ---- the dominant kernel alone (roofline): the attention grid without the
     # merge grid (DSA_ATTN_STAGE=1), captured and timed the same way
     os.environ["DSA_ATTN_STAGE"] = "1"
-    g_attn = torch.cuda.CUDAGraph()
     with torch.cuda.stream(side):
-        kernel(qn, qp, ckv, kpe, idx, scale, output=out, lse=lse)
-        with torch.cuda.graph(g_attn, stream=side):
-            kernel(qn, qp, ckv, kpe, idx, scale, output=out, lse=lse)
-    stream.wait_stream(side)
+        op()
+    attn_ms = graph_timed_steps(op, min(args.steps, 200), flush, side, stream)
     os.environ.pop("DSA_ATTN_STAGE")
-    attn_ms = []
-    for i in range(min(args.steps, 200)):
-        flush(i)
-        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s0.record(stream)
-        g_attn.replay()
-        s1.record(stream)
-        s1.synchronize()
-        attn_ms.append(s0.elapsed_time(s1))
     attn_kernel_ms = statistics.mean(attn_ms)
     kernel(qn, qp, ckv, kpe, idx, scale, output=out, lse=lse)  # leave complete results
 
-    # ---- end to end through the public API with host buffers.  Two steps are
-    # in flight, as in a serving loop: the next step's queries and indices go
-    # up on an upload stream while this step computes, its output comes back
-    # on a download stream.  Every step includes its own copies.  Steps
+    # ---- end to end through the public API with host buffers: every step
+    # uploads its queries and indices from pinned host memory, runs the
+    # operator and downloads output + LSE.  Three streams form a pipeline
+    # (upload of step i+1 and download of step i-1 under the compute of step
+    # i), each replaying a per-buffer CUDA graph of its part (the captured
+    # copies and kernel() call); four buffer sets, ordered by events.  Steps
     # alternate between two independent batches (two 2.1 GB caches), so the
     # rows gathered by consecutive steps (2 x 151 MB) do not fit in L2.
+    NB = 4
     qn2, qp2, ckv2, kpe2, idx2, _ = make_cfg2_device(seed=5000 + rank, device=dev)
     batches = [(qn, qp, ckv, kpe, idx), (qn2, qp2, ckv2, kpe2, idx2)]
-    host = [tuple(t.cpu().pin_memory() for t in (b_[0], b_[1], b_[4])) for b_ in batches]
-    dbuf = [tuple(torch.empty_like(t) for t in (b_[0], b_[1], b_[4])) for b_ in batches]
-    h_out = [torch.empty(out.shape, dtype=out.dtype).pin_memory() for _ in range(2)]
-    h_lse = [torch.empty(lse.shape, dtype=lse.dtype).pin_memory() for _ in range(2)]
-    d_out = [torch.empty_like(out) for _ in range(2)]
-    d_lse = [torch.empty_like(lse) for _ in range(2)]
-    h2d = sum(t.numel() * t.element_size() for t in host[0])
+    # a step's inputs sit in one pinned staging buffer (q_nope | q_pe | indices,
+    # 256-byte aligned parts), uploaded with one copy into a device buffer whose
+    # typed views are the operator's arguments
+    def layout(ts):
+        offs, o = [], 0
+        for t in ts:
+            offs.append(o)
+            o += (t.numel() * t.element_size() + 255) // 256 * 256
+        return offs, o
+
+    def views(buf, ts, offs):
+        return tuple(buf[o:o + t.numel() * t.element_size()].view(t.dtype).view(t.shape)
+                     for t, o in zip(ts, offs))
+    host_in = []
+    for b_ in batches:
+        ts = (b_[0], b_[1], b_[4])
+        offs, nbytes = layout(ts)
+        hb = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+        for t, v in zip(ts, views(hb, ts, offs)):
+            v.copy_(t.cpu())
+        host_in.append((hb, ts, offs))
+    host = [host_in[b_ % 2][0] for b_ in range(NB)]
+    dstage = [torch.empty(h.numel(), dtype=torch.uint8, device=dev) for h in host]
+    dbuf = [views(dstage[b_], host_in[b_ % 2][1], host_in[b_ % 2][2]) for b_ in range(NB)]
+    h_out = [torch.empty(out.shape, dtype=out.dtype).pin_memory() for _ in range(NB)]
+    h_lse = [torch.empty(lse.shape, dtype=lse.dtype).pin_memory() for _ in range(NB)]
+    d_out = [torch.empty_like(out) for _ in range(NB)]
+    d_lse = [torch.empty_like(lse) for _ in range(NB)]
+    h2d = host[0].numel()
     d2h = h_out[0].numel() * 2 + h_lse[0].numel() * 4
     up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    up_done = [torch.cuda.Event() for _ in range(2)]
-    comp_done = [torch.cuda.Event() for _ in range(2)]
-    down_done = [torch.cuda.Event() for _ in range(2)]
+
+    def part_up(b_):
+        dstage[b_].copy_(host[b_], non_blocking=True)
+
+    def part_comp(b_):
+        cb = batches[b_ % 2]
+        kernel(dbuf[b_][0], dbuf[b_][1], cb[2], cb[3], dbuf[b_][2], scale, output=d_out[b_],
+               lse=d_lse[b_])
+
+    def part_down(b_):
+        h_out[b_].copy_(d_out[b_], non_blocking=True)
+        h_lse[b_].copy_(d_lse[b_], non_blocking=True)
+    g_parts = []
+    cap = torch.cuda.Stream(dev)
+    cap.wait_stream(stream)
+    with torch.cuda.stream(cap):
+        for b_ in range(NB):
+            part_up(b_)
+            part_comp(b_)
+            part_down(b_)
+        torch.cuda.synchronize()
+        for b_ in range(NB):
+            trio = []
+            for fn in (part_up, part_comp, part_down):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=cap):
+                    fn(b_)
+                trio.append(g)
+            g_parts.append(trio)
+    torch.cuda.synchronize()
+    up_done = [torch.cuda.Event() for _ in range(NB)]
+    comp_done = [torch.cuda.Event() for _ in range(NB)]
+    down_done = [torch.cuda.Event() for _ in range(NB)]
 
     def e2e_steps(n):
         for i in range(n):
-            b_ = i & 1
+            b_ = i % NB
+            if i >= NB:
+                up.wait_event(comp_done[b_])       # inputs of step i-NB consumed
             with torch.cuda.stream(up):
-                up.wait_event(comp_done[b_])      # inputs of step i-2 consumed
-                for d_, h_ in zip(dbuf[b_], host[b_]):
-                    d_.copy_(h_, non_blocking=True)
-                up_done[b_].record(up)
+                g_parts[b_][0].replay()
+            up_done[b_].record(up)
             stream.wait_event(up_done[b_])
-            stream.wait_event(down_done[b_])      # outputs of step i-2 downloaded
-            kernel(dbuf[b_][0], dbuf[b_][1], batches[b_][2], batches[b_][3], dbuf[b_][2], scale,
-                   output=d_out[b_], lse=d_lse[b_])
+            if i >= NB:
+                stream.wait_event(down_done[b_])  # outputs of step i-NB downloaded
+            g_parts[b_][1].replay()
             comp_done[b_].record(stream)
+            down.wait_event(comp_done[b_])
             with torch.cuda.stream(down):
-                down.wait_event(comp_done[b_])
-                h_out[b_].copy_(d_out[b_], non_blocking=True)
-                h_lse[b_].copy_(d_lse[b_], non_blocking=True)
-                down_done[b_].record(down)
+                g_parts[b_][2].replay()
+            down_done[b_].record(down)
 
-    e2e_steps(args.warmup)
+    e2e_steps(max(args.warmup, NB))
     torch.cuda.synchronize()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_start.record(up)
+    e_start.record(stream)
+    up.wait_event(e_start)
+    down.wait_event(e_start)
     e2e_steps(args.steps)
     e_end.record(down)
     torch.cuda.synchronize()
-    e2e_eager = e_start.elapsed_time(e_end)
-
-    # the same steps with each buffer's upload + operator + download captured
-    # once as a CUDA graph; the two graphs alternate on two streams
-    gstreams = [torch.cuda.Stream(dev) for _ in range(2)]
-    graphs = []
-    for b_ in range(2):
-        g = torch.cuda.CUDAGraph()
-        gstreams[b_].wait_stream(stream)
-        with torch.cuda.stream(gstreams[b_]):
-            with torch.cuda.graph(g, stream=gstreams[b_]):
-                for d_, h_ in zip(dbuf[b_], host[b_]):
-                    d_.copy_(h_, non_blocking=True)
-                kernel(dbuf[b_][0], dbuf[b_][1], batches[b_][2], batches[b_][3], dbuf[b_][2], scale,
-                       output=d_out[b_], lse=d_lse[b_])
-                h_out[b_].copy_(d_out[b_], non_blocking=True)
-                h_lse[b_].copy_(d_lse[b_], non_blocking=True)
-        graphs.append(g)
-    torch.cuda.synchronize()
-    for i in range(args.warmup):
-        with torch.cuda.stream(gstreams[i & 1]):
-            graphs[i & 1].replay()
-    torch.cuda.synchronize()
-    g_start = torch.cuda.Event(enable_timing=True)
-    g_end = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-    g_start.record(stream)
-    for s_ in gstreams:
-        s_.wait_event(g_start)
-    for i in range(args.steps):
-        with torch.cuda.stream(gstreams[i & 1]):
-            graphs[i & 1].replay()
-    for b_ in range(2):
-        g_end[b_].record(gstreams[b_])
-    torch.cuda.synchronize()
-    e2e_graph = max(g_start.elapsed_time(e) for e in g_end)
-    e2e_total = min(e2e_eager, e2e_graph)
-    ok = torch.equal(h_out[(args.steps - 1) & 1].to(dev), d_out[(args.steps - 1) & 1])
+    e2e_total = e_start.elapsed_time(e_end)
+    last = (args.steps - 1) % NB
+    ok = torch.equal(h_out[last].to(dev), d_out[last])
     if read_device_error(dev) or not ok:
         raise SystemExit("device error flag set, or downloaded output differs, during the timed steps")
 
@@ -384,7 +414,7 @@ def run_ours(args):
             "data": "synthetic (seeded, BASELINE cfg2 shapes and distributions)",
             "config": {"workload": WORKLOAD, "tokens_per_gpu": T, "parallelism": f"request-shard x{world}",
                        "l2": L2_NOTE,
-                       "launch": "value: CUDA-graph replay of the operator call; e2e: eager Python API",
+                       "launch": "value: steps as nodes of a CUDA graph (50 per graph), each step timed by its own event pair on the device; e2e: the public API with host copies",
                        "alg_bytes_per_step_per_gpu": alg_bytes},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": ATTN_TRAFFIC_PER_LAUNCH,
@@ -395,11 +425,15 @@ def run_ours(args):
                          "step_frac": alg_bytes / (statistics.mean(step_ms) / 1e3) / 1e9 / peak},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
-                    "eager_ms_per_step": e2e_eager / args.steps, "graph_ms_per_step": e2e_graph / args.steps,
-                    "note": "kernel() with pinned host buffers, 2 steps in flight, alternating two "
-                            "batches (inputs larger than L2); value = faster of the eager loop "
-                            "(upload/compute/download streams) and per-step CUDA graphs "
-                            "(upload + operator + download captured, replayed on 2 streams)"},
+                    "ms_per_step": e2e_total / args.steps,
+                    "pcie_floor_ms_per_step": h2d / 55e9 * 1e3,
+                    "note": "kernel() with pinned host buffers: per step the upload of q_nope, "
+                            "q_pe and sparse_indices (one staging buffer, one copy), the operator, "
+                            "and the download of output + "
+                            "LSE, pipelined over upload/compute/download streams (per-buffer CUDA "
+                            "graphs of each part, 4 buffer sets), alternating two batches (inputs "
+                            "larger than L2); pcie_floor = upload bytes at the 55 GB/s measured "
+                            "for pinned copies on this host"},
             "gpu_launches": 2 * args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,
