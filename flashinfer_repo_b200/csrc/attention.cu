@@ -42,6 +42,7 @@ constexpr int kDp = 64;
 constexpr int kRows = 32;             // rows per tile
 constexpr int kCkvStride = 1040;      // smem pitch of a 1024-B ckv row
 constexpr int kKpeStride = 144;       // smem pitch of a 128-B kpe row
+constexpr float kLazyLog2 = 8.f;     // lazy-rescale threshold (log2 units)
 constexpr int kCWarps = 4;            // consumer warps
 constexpr int kPWarps = 2;            // producer warps
 constexpr int kThreads = (kCWarps + kPWarps) * 32;
@@ -363,49 +364,66 @@ __global__ void __launch_bounds__(kThreads, (NST == 2 ? 2 : 1)) dsa_attention_ke
       }
       buf ^= 1;
 
-      // ---- online softmax (base 2), rows g and g+8
+      // ---- online softmax (base 2), heads g and g+8
       uint32_t vm = 0;
 #pragma unroll
       for (int q = 0; q < kPWarps; ++q) vm |= S.vmask[s][q];
       float mx0 = -INFINITY, mx1 = -INFINITY;
+      if (vm == 0xffffffffu) {  // no padding row in this tile (the usual case)
 #pragma unroll
-      for (int nb = 0; nb < 4; ++nb) {
+        for (int nb = 0; nb < 4; ++nb) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int col = nb * 8 + 2 * c + (e & 1);
-          x[nb][e] = ((vm >> col) & 1u) ? x[nb][e] * p.scale_log2 : -INFINITY;
+          for (int e = 0; e < 4; ++e) x[nb][e] *= p.scale_log2;
+          mx0 = fmaxf(mx0, fmaxf(x[nb][0], x[nb][1]));
+          mx1 = fmaxf(mx1, fmaxf(x[nb][2], x[nb][3]));
         }
-        mx0 = fmaxf(mx0, fmaxf(x[nb][0], x[nb][1]));
-        mx1 = fmaxf(mx1, fmaxf(x[nb][2], x[nb][3]));
+      } else {
+#pragma unroll
+        for (int nb = 0; nb < 4; ++nb) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int col = nb * 8 + 2 * c + (e & 1);
+            x[nb][e] = ((vm >> col) & 1u) ? x[nb][e] * p.scale_log2 : -INFINITY;
+          }
+          mx0 = fmaxf(mx0, fmaxf(x[nb][0], x[nb][1]));
+          mx1 = fmaxf(mx1, fmaxf(x[nb][2], x[nb][3]));
+        }
       }
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-      const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
-      const float a0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - n0);
-      const float a1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - n1);
-      m0 = n0;
-      m1 = n1;
+      // Lazy rescaling: the maximum used for the exponentials moves only when
+      // a tile's maximum exceeds it by more than kLazyLog2 (a factor 2^8), so
+      // P stays <= 256 and O, l are rescaled on few tiles.
+      const bool up0 = mx0 > m0 + kLazyLog2, up1 = mx1 > m1 + kLazyLog2;
+      if (__any_sync(0xffffffffu, up0 || up1)) {
+        const float a0 = up0 ? ((m0 == -INFINITY) ? 0.f : ex2_approx(m0 - mx0)) : 1.f;
+        const float a1 = up1 ? ((m1 == -INFINITY) ? 0.f : ex2_approx(m1 - mx1)) : 1.f;
+        if (up0) m0 = mx0;
+        if (up1) m1 = mx1;
+        l0 *= a0;
+        l1 *= a1;
+#pragma unroll
+        for (int nb = 0; nb < 16; ++nb) {
+          o[nb][0] *= a0;
+          o[nb][1] *= a0;
+          o[nb][2] *= a1;
+          o[nb][3] *= a1;
+        }
+      }
       float rs0 = 0.f, rs1 = 0.f;
 #pragma unroll
       for (int nb = 0; nb < 4; ++nb) {
-        x[nb][0] = (n0 == -INFINITY) ? 0.f : exp2f(x[nb][0] - n0);
-        x[nb][1] = (n0 == -INFINITY) ? 0.f : exp2f(x[nb][1] - n0);
-        x[nb][2] = (n1 == -INFINITY) ? 0.f : exp2f(x[nb][2] - n1);
-        x[nb][3] = (n1 == -INFINITY) ? 0.f : exp2f(x[nb][3] - n1);
+        x[nb][0] = (m0 == -INFINITY) ? 0.f : ex2_approx(x[nb][0] - m0);
+        x[nb][1] = (m0 == -INFINITY) ? 0.f : ex2_approx(x[nb][1] - m0);
+        x[nb][2] = (m1 == -INFINITY) ? 0.f : ex2_approx(x[nb][2] - m1);
+        x[nb][3] = (m1 == -INFINITY) ? 0.f : ex2_approx(x[nb][3] - m1);
         rs0 += x[nb][0] + x[nb][1];
         rs1 += x[nb][2] + x[nb][3];
       }
-      l0 = l0 * a0 + rs0;
-      l1 = l1 * a1 + rs1;
-#pragma unroll
-      for (int nb = 0; nb < 16; ++nb) {
-        o[nb][0] *= a0;
-        o[nb][1] *= a0;
-        o[nb][2] *= a1;
-        o[nb][3] *= a1;
-      }
+      l0 += rs0;
+      l1 += rs1;
       uint32_t pa[2][4];
 #pragma unroll
       for (int kj = 0; kj < 2; ++kj) {
