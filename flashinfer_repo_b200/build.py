@@ -74,5 +74,23 @@ def build(force: bool = False, verbose: bool = False) -> str:
     return LIB
 
 
+def build_contest_binding(force: bool = False) -> str | None:
+    """Compile the contest route's TVM-FFI binding (contest/binding.cu) for
+    sm_100a into _build/ as a check that it builds; the contest harness itself
+    compiles the packed sources with tvm_ffi.cpp.load.  Skipped (None) when
+    tvm_ffi is not installed."""
+    try:
+        import tvm_ffi
+    except ImportError:
+        return None
+    src = os.path.join(PKG, "contest", "binding.cu")
+    obj = os.path.join(BUILD_DIR, "contest_binding.o")
+    os.makedirs(BUILD_DIR, exist_ok=True)
+    if force or _stale(obj, [src, os.path.join(INCLUDE, "dsa_b200.h")]):
+        inc = os.path.join(os.path.dirname(tvm_ffi.__file__), "include")
+        subprocess.check_call([nvcc()] + NVCC_FLAGS + ["-I", ROOT, "-I", inc, "-c", src, "-o", obj])
+    return obj
+
+
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))
