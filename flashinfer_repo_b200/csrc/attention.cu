@@ -73,7 +73,6 @@ struct AttnParams {
   float* lse_peers[kMaxTargets];
   int n_peers;
   float* part;
-  int* counters;
   int* err;
 };
 
@@ -1020,7 +1019,7 @@ int make_plan(int64_t num_tokens, int64_t heads, int64_t topk, int nst, Plan* pl
   pl->ctas = (int)ctas;
   pl->base = (int)(pl->total_tiles / ctas);
   pl->rem = (int)(pl->total_tiles % ctas);
-  pl->part_off = align256(256 + 4 * (size_t)pl->vtokens);
+  pl->part_off = 256;  // error word, then the split-K partials
   pl->bytes = pl->part_off + (size_t)pl->ctas * 2 * kPartFloats * sizeof(float);
   return DSA_OK;
 }
@@ -1129,7 +1128,6 @@ static int attention_impl(const void* q_nope, int64_t q_nope_stride_token, int64
   p.tiles_rem = pl.rem;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   p.err = reinterpret_cast<int*>(ws);
-  p.counters = reinterpret_cast<int*>(ws + 256);
   p.part = reinterpret_cast<float*>(ws + pl.part_off);
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -6,8 +6,8 @@
 // there fails or breaks their accounting), and plugin hosts whose interface
 // hands an operator only its input and output buffers, with no workspace
 // argument and no allocator to call.  For them this entry point runs the same
-// kernel as dsa_sparse_attention with its scratch (error word, per-token
-// arrival counters, split-K partials) in a fixed-size array that lives in the
+// kernel as dsa_sparse_attention with its scratch (error word, split-K
+// partials) in a fixed-size array that lives in the
 // library's own device memory.
 //
 // Facts a caller must know:
@@ -22,7 +22,7 @@
 //  * All calls on a device share the one array and it keeps the last call's
 //    contents.  Calls whose executions overlap on the GPU (different streams,
 //    or several host threads) race on it and give wrong results; serialise
-//    them.  Each call clears the error word and the counters it uses.
+//    them.  Each call clears the error word.
 //  * No cudaMalloc, cudaFree or other allocating routine is called.
 #include <mutex>
 
@@ -34,7 +34,7 @@ namespace {
 constexpr size_t kNoAllocMaxVirtualTokens = 8192;
 constexpr size_t kNoAllocMaxCtas = 320;
 constexpr size_t kPartBytes = (16 * 512 + 2 * 16) * sizeof(float);  // one split-K partial
-constexpr size_t kCounterBytes = 256 + 4 * kNoAllocMaxVirtualTokens;  // error word + counters
+constexpr size_t kCounterBytes = 256;  // error word
 constexpr size_t kNoAllocScratchBytes = kCounterBytes + 2 * kNoAllocMaxCtas * kPartBytes;
 
 // Zero-initialised at module load; one instance per device.
@@ -98,8 +98,8 @@ extern "C" int dsa_sparse_attention_noalloc(
                             "dsa_sparse_attention_noalloc: this shape needs more split-K scratch "
                             "than the static array holds; use dsa_sparse_attention");
 
-  // Error word and this call's counters start at zero.
-  e = cudaMemsetAsync(scratch, 0, 256 + 4 * (size_t)vtokens, static_cast<cudaStream_t>(stream));
+  // The error word starts at zero.
+  e = cudaMemsetAsync(scratch, 0, sizeof(int), static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return dsa_noalloc_fail(DSA_ERR_CUDA, cudaGetErrorString(e));
 
   return dsa_sparse_attention(q_nope, q_nope_stride_token, q_nope_stride_head, q_pe,

@@ -26,24 +26,17 @@ TOPK = 2048
 
 
 class _Workspace:
-    """Per-device persistent workspace (error word, per-token counters,
-    split-K partials).  Zero-filled when allocated; the kernel leaves its
-    counters at zero, and the counter region is re-zeroed on the stream when
-    a call needs more counters than any earlier call on this buffer."""
+    """Per-device persistent workspace: the device error word (zeroed when
+    allocated, cleared by read_device_error) followed by split-K partials."""
 
     def __init__(self):
         self.buf = None
-        self.max_vtokens = 0
         self.lock = threading.Lock()
 
     def get(self, device, nbytes, vtokens, stream):
         with self.lock:
             if self.buf is None or self.buf.numel() < nbytes:
                 self.buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
-                self.max_vtokens = 0
-            if vtokens > self.max_vtokens:
-                self.buf[256: 256 + 4 * vtokens].zero_()
-                self.max_vtokens = vtokens
             return self.buf
 
 

@@ -74,10 +74,11 @@ int dsa_sparse_attention_workspace_size(int64_t num_tokens, int64_t num_heads, i
  * independent 16-head groups sharing the same indices).
  *
  * workspace: >= dsa_sparse_attention_workspace_size() bytes, 256-byte aligned,
- * ZERO-FILLED before its first use (and again if it is reused for a larger
- * num_tokens*num_heads).  Every call leaves its counters at zero, so the same
- * workspace can be reused by later calls on the same stream.  Calls that
- * share one workspace must not overlap in time.
+ * its first int zero before the first use (the device error word, cleared by
+ * dsa_read_device_error; the rest holds split-K partials and needs no
+ * initialisation).  The same workspace can be reused by later calls of any
+ * size on the same stream; calls that share one workspace must not overlap
+ * in time.
  */
 int dsa_sparse_attention(const void* q_nope, int64_t q_nope_stride_token, int64_t q_nope_stride_head,
                          const void* q_pe, int64_t q_pe_stride_token, int64_t q_pe_stride_head,
