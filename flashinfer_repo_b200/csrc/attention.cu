@@ -42,6 +42,7 @@ constexpr int kDp = 64;
 constexpr int kRows = 32;             // rows per tile
 constexpr int kCkvStride = 1040;      // smem pitch of a 1024-B ckv row
 constexpr int kKpeStride = 144;       // smem pitch of a 128-B kpe row
+constexpr int kPPitch = 40;           // P tile row pitch (bf16): 80 B, conflict-free ldmatrix
 constexpr float kLazyLog2 = 8.f;     // lazy-rescale threshold (log2 units)
 constexpr int kCWarps = 4;            // consumer warps
 constexpr int kPWarps = 2;            // producer warps
@@ -81,6 +82,9 @@ struct AttnSmem {
   uint8_t ckv[NST][kRows * kCkvStride];
   uint8_t kpe[NST][kRows * kKpeStride];
   float4 sred[2][kCWarps][4][32];  // [buf][warp][n-block][lane]: conflict-free
+  float smax[2][kHeads][kCWarps];  // [buf][head][warp]: per-warp row-block maxima
+  __nv_bfloat16 pbuf[2][kHeads][kPPitch];  // [buf][head][row]: P (bf16) for the PV A operand
+  float lred[kCWarps][kHeads];     // per-warp normalisers, summed at segment ends
   uint32_t vmask[NST][kPWarps];  // valid-row bits, one word per producer warp
   uint64_t full[NST];
   uint64_t empty[NST];
@@ -347,54 +351,46 @@ __global__ void __launch_bounds__(kThreads, (NST == 2 ? 2 : 1)) dsa_attention_ke
       for (int nb = 0; nb < 4; ++nb)
         S.sred[buf][warp][nb][lane] = make_float4(sc[nb][0], sc[nb][1], sc[nb][2], sc[nb][3]);
       named_bar_sync(1, kCWarps * 32);
-      float x[4][4];
+      // ---- softmax, split by rows: warp w owns rows 8w..8w+7 of the tile (its
+      // n-block of S, summed over the four quarters); x[0], x[1] are head g at
+      // rows 8w+2c, +1 and x[2], x[3] head g+8
+      float x[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int nb = 0; nb < 4; ++nb) x[nb][0] = x[nb][1] = x[nb][2] = x[nb][3] = 0.f;
-#pragma unroll
-      for (int w = 0; w < kCWarps; ++w) {
-#pragma unroll
-        for (int nb = 0; nb < 4; ++nb) {
-          const float4 a = S.sred[buf][w][nb][lane];
-          x[nb][0] += a.x;
-          x[nb][1] += a.y;
-          x[nb][2] += a.z;
-          x[nb][3] += a.w;
-        }
+      for (int q = 0; q < kCWarps; ++q) {
+        const float4 a = S.sred[buf][q][warp][lane];
+        x[0] += a.x;
+        x[1] += a.y;
+        x[2] += a.z;
+        x[3] += a.w;
       }
-      buf ^= 1;
-
-      // ---- online softmax (base 2), heads g and g+8
       uint32_t vm = 0;
 #pragma unroll
       for (int q = 0; q < kPWarps; ++q) vm |= S.vmask[s][q];
-      float mx0 = -INFINITY, mx1 = -INFINITY;
-      if (vm == 0xffffffffu) {  // no padding row in this tile (the usual case)
-#pragma unroll
-        for (int nb = 0; nb < 4; ++nb) {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) x[nb][e] *= p.scale_log2;
-          mx0 = fmaxf(mx0, fmaxf(x[nb][0], x[nb][1]));
-          mx1 = fmaxf(mx1, fmaxf(x[nb][2], x[nb][3]));
-        }
-      } else {
-#pragma unroll
-        for (int nb = 0; nb < 4; ++nb) {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int col = nb * 8 + 2 * c + (e & 1);
-            x[nb][e] = ((vm >> col) & 1u) ? x[nb][e] * p.scale_log2 : -INFINITY;
-          }
-          mx0 = fmaxf(mx0, fmaxf(x[nb][0], x[nb][1]));
-          mx1 = fmaxf(mx1, fmaxf(x[nb][2], x[nb][3]));
-        }
-      }
+      const uint32_t vb = vm >> (8 * warp + 2 * c);
+      x[0] = (vb & 1u) ? x[0] * p.scale_log2 : -INFINITY;
+      x[1] = (vb & 2u) ? x[1] * p.scale_log2 : -INFINITY;
+      x[2] = (vb & 1u) ? x[2] * p.scale_log2 : -INFINITY;
+      x[3] = (vb & 2u) ? x[3] * p.scale_log2 : -INFINITY;
+      float mx0 = fmaxf(x[0], x[1]), mx1 = fmaxf(x[2], x[3]);
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      if (c == 0) {
+        S.smax[buf][g][warp] = mx0;
+        S.smax[buf][g + 8][warp] = mx1;
+      }
+      named_bar_sync(1, kCWarps * 32);
+      {
+        const float4 a = *reinterpret_cast<const float4*>(&S.smax[buf][g][0]);
+        const float4 b = *reinterpret_cast<const float4*>(&S.smax[buf][g + 8][0]);
+        mx0 = fmaxf(fmaxf(a.x, a.y), fmaxf(a.z, a.w));
+        mx1 = fmaxf(fmaxf(b.x, b.y), fmaxf(b.z, b.w));
+      }
       // Lazy rescaling: the maximum used for the exponentials moves only when
-      // a tile's maximum exceeds it by more than kLazyLog2 (a factor 2^8), so
-      // P stays <= 256 and O, l are rescaled on few tiles.
+      // the tile's maximum exceeds it by more than kLazyLog2 (a factor 2^8), so
+      // P stays <= 256 and O, l are rescaled on few tiles.  Every warp sees the
+      // same maxima and takes the same decisions.
       const bool up0 = mx0 > m0 + kLazyLog2, up1 = mx1 > m1 + kLazyLog2;
       if (__any_sync(0xffffffffu, up0 || up1)) {
         const float a0 = up0 ? ((m0 == -INFINITY) ? 0.f : ex2_approx(m0 - mx0)) : 1.f;
@@ -411,26 +407,25 @@ __global__ void __launch_bounds__(kThreads, (NST == 2 ? 2 : 1)) dsa_attention_ke
           o[nb][3] *= a1;
         }
       }
-      float rs0 = 0.f, rs1 = 0.f;
-#pragma unroll
-      for (int nb = 0; nb < 4; ++nb) {
-        x[nb][0] = (m0 == -INFINITY) ? 0.f : ex2_approx(x[nb][0] - m0);
-        x[nb][1] = (m0 == -INFINITY) ? 0.f : ex2_approx(x[nb][1] - m0);
-        x[nb][2] = (m1 == -INFINITY) ? 0.f : ex2_approx(x[nb][2] - m1);
-        x[nb][3] = (m1 == -INFINITY) ? 0.f : ex2_approx(x[nb][3] - m1);
-        rs0 += x[nb][0] + x[nb][1];
-        rs1 += x[nb][2] + x[nb][3];
-      }
-      l0 += rs0;
-      l1 += rs1;
+      x[0] = (m0 == -INFINITY) ? 0.f : ex2_approx(x[0] - m0);
+      x[1] = (m0 == -INFINITY) ? 0.f : ex2_approx(x[1] - m0);
+      x[2] = (m1 == -INFINITY) ? 0.f : ex2_approx(x[2] - m1);
+      x[3] = (m1 == -INFINITY) ? 0.f : ex2_approx(x[3] - m1);
+      l0 += x[0] + x[1];  // this thread's rows only; summed at the segment end
+      l1 += x[2] + x[3];
+      *reinterpret_cast<uint32_t*>(&S.pbuf[buf][g][8 * warp + 2 * c]) = pack_bf16(x[0], x[1]);
+      *reinterpret_cast<uint32_t*>(&S.pbuf[buf][g + 8][8 * warp + 2 * c]) = pack_bf16(x[2], x[3]);
+      named_bar_sync(1, kCWarps * 32);
+      // P [16 heads x 32 rows] as the m16n8k16 A operand, two k-steps of 16 rows
       uint32_t pa[2][4];
+      {
+        const uint32_t pbase = smem_u32(&S.pbuf[buf][0][0]);
 #pragma unroll
-      for (int kj = 0; kj < 2; ++kj) {
-        pa[kj][0] = pack_bf16(x[2 * kj][0], x[2 * kj][1]);
-        pa[kj][1] = pack_bf16(x[2 * kj][2], x[2 * kj][3]);
-        pa[kj][2] = pack_bf16(x[2 * kj + 1][0], x[2 * kj + 1][1]);
-        pa[kj][3] = pack_bf16(x[2 * kj + 1][2], x[2 * kj + 1][3]);
+        for (int kj = 0; kj < 2; ++kj)
+          ldsm_x4(pbase + ((lane & 15) * kPPitch + 16 * kj + (lane >> 4) * 8) * 2, pa[kj][0], pa[kj][1],
+                  pa[kj][2], pa[kj][3]);
       }
+      buf ^= 1;
 
       // ---- PV: this warp's 128 output columns
 #pragma unroll
@@ -451,11 +446,20 @@ __global__ void __launch_bounds__(kThreads, (NST == 2 ? 2 : 1)) dsa_attention_ke
     }
     if (!ok) break;
 
-    // ---- finish this (token, segment)
+    // ---- finish this (token, segment): normalisers summed over the quad
+    // (rows of this warp) and over the four warps
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
     l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    if (c == 0) {
+      S.lred[warp][g] = l0;
+      S.lred[warp][g + 8] = l1;
+    }
+    named_bar_sync(1, kCWarps * 32);
+    l0 = S.lred[0][g] + S.lred[1][g] + S.lred[2][g] + S.lred[3][g];
+    l1 = S.lred[0][g + 8] + S.lred[1][g + 8] + S.lred[2][g + 8] + S.lred[3][g + 8];
+    named_bar_sync(1, kCWarps * 32);  // S.lred is rewritten at the next segment end
     const int c_first = cta_of_tile(p, v * tpt);
     const int c_last = cta_of_tile(p, v * tpt + tpt - 1);
     if (c_first == c_last) {
