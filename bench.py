@@ -38,8 +38,7 @@ sys.path.insert(0, ROOT)
 METRIC = "DSA decode query-tokens/sec (whole job); achieved HBM GB/s vs B200 peak"
 UNIT = "query_tokens/s"
 # dram__bytes_read.sum + dram__bytes_write.sum of one dsa_attention_kernel launch on
-# this workload (medians over 24 launches of the committed ncu launch list,
-# profiles/dsa_attention_kernel_cfg2.md)
+# this workload: medians over 24 launches of an ncu launch list of this command
 ATTN_TRAFFIC_PER_LAUNCH = 153_366_784 + 1_001_984
 WORKLOAD = ("cfg2 batched decode: T=64 tokens/GPU, 16 heads, ckv512+kpe64 bf16, page 64, "
             "ctx U[1024,65536], topk 2048 (-1 padded), shuffled page tables")
