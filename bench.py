@@ -64,6 +64,34 @@ class L2Flush:
         torch.sum(self.r, dim=0, out=self.acc)
 
 
+def bind_to_gpu_numa(device_index: int) -> str:
+    """Run this process on the CPUs of the NUMA node the GPU's PCIe link
+    attaches to (read from sysfs through the GPU's PCI bus id), so that pinned
+    host buffers allocated afterwards are local to that link.  Returns a short
+    description for the JSON line; leaves the affinity alone when the topology
+    cannot be read."""
+    try:
+        pr = torch.cuda.get_device_properties(device_index)
+        bdf = f"{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        with open(f"/sys/bus/pci/devices/{bdf}/numa_node") as f:
+            node = int(f.read().strip())
+        if node < 0:
+            return f"gpu {bdf}: no NUMA node reported, affinity unchanged"
+        with open(f"/sys/devices/system/node/node{node}/cpulist") as f:
+            spec = f.read().strip()
+        cpus = set()
+        for part in spec.split(","):
+            a, _, b = part.partition("-")
+            cpus.update(range(int(a), int(b or a) + 1))
+        cpus &= os.sched_getaffinity(0)
+        if not cpus:
+            return f"gpu {bdf}: node {node} CPUs not available, affinity unchanged"
+        os.sched_setaffinity(0, cpus)
+        return f"gpu {bdf} on NUMA node {node}: process bound to its {len(cpus)} CPUs"
+    except (OSError, ValueError, AttributeError) as e:
+        return f"affinity unchanged ({type(e).__name__})"
+
+
 def graph_timed_steps(fn, steps, flush, side, stream, per_graph=50):
     """Device time (ms) of each of `steps` calls of fn(), run as CUDA-graph
     nodes: every captured step is flush(), a start event, fn(), an end event
@@ -229,6 +257,8 @@ def run_ours(args):
     rank, world, local = dist_setup(args.gpus)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    all_cpus = os.sched_getaffinity(0)
+    numa = bind_to_gpu_numa(local)
     dist = None
     if world > 1:
         import torch.distributed as dist
@@ -450,6 +480,7 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        os.sched_setaffinity(0, all_cpus)  # the CPU baseline uses every host core
         v, cores, sample = cpu_baseline_run(qn, qp, ckv, kpe, idx, scale)
         cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
 
@@ -473,6 +504,7 @@ def run_ours(args):
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_total / args.steps,
+                    "host_numa": numa,
                     "host_driven_ms_per_step": e2e_a / args.steps,
                     "one_graph_ms_per_step": e2e_b / args.steps,
                     "pcie_floor_ms_per_step": h2d / 55e9 * 1e3,
@@ -681,6 +713,8 @@ def run_cfg5(args):
     rank, world, local = dist_setup(args.gpus)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    all_cpus = os.sched_getaffinity(0)
+    numa = bind_to_gpu_numa(local)
     dist = None
     if world > 1:
         import torch.distributed as dist
