@@ -106,6 +106,18 @@ def test_signatures_cover_declarations():
     assert set(_declared_symbols()) == set(_lib.SIGNATURES) | {"dsa_last_error_message"}
 
 
+def test_signature_argument_counts_match_header():
+    """Every ctypes argtypes list has as many entries as the header declaration
+    has parameters (guards against an ABI change on one side only)."""
+    src = open(os.path.join(ROOT, "include", "dsa_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    decls = dict(re.findall(r"\b(dsa_[a-z0-9_]+)\s*\(([^;]*?)\)\s*;", src, flags=re.S))
+    for name, argtypes in _lib.SIGNATURES.items():
+        params = decls[name].strip()
+        n = 0 if params in ("", "void") else params.count(",") + 1
+        assert n == len(argtypes), f"{name}: header has {n} parameters, ctypes table {len(argtypes)}"
+
+
 def test_abi_argument_validation_without_gpu():
     lib = _lib.load()
     n = ctypes.c_size_t(0)
