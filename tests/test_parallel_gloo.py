@@ -1,4 +1,4 @@
-"""Multi-process host logic on CPU (gloo, world size 2): request sharding,
+"""Multi-process host logic on CPU (gloo, world sizes 2-4): request sharding,
 head sharding with the packed all-gather, and failure detection (a rank that
 leaves before the collective makes the others fail within the process-group
 timeout instead of hanging).  The local 16-head operator is the C oracle
@@ -99,10 +99,11 @@ def test_shard_range_covers_everything():
             assert max(sizes) - min(sizes) <= 1
 
 
-def test_head_sharded_all_gather_matches_full_operator():
-    res = _run("heads")
-    case = W.make_attention_case(77, [5000, 3000, 9000], heads=32, shared_cache=True)
-    for g in range(2):
+@pytest.mark.parametrize("world", [2, 4])
+def test_head_sharded_all_gather_matches_full_operator(world):
+    res = _run("heads", world)
+    case = W.make_attention_case(77, [5000, 3000, 9000], heads=16 * world, shared_cache=True)
+    for g in range(world):
         sl = slice(16 * g, 16 * g + 16)
         ref_out, ref_lse = O.dsa_attention(case.q_nope[:, sl], case.q_pe[:, sl], case.ckv, case.kpe,
                                            case.idx, case.sm_scale)
@@ -111,8 +112,9 @@ def test_head_sharded_all_gather_matches_full_operator():
             assert np.array_equal(lse[:, sl], ref_lse)
 
 
-def test_request_sharding_is_exact_partition():
-    res = _run("requests")
+@pytest.mark.parametrize("world", [2, 3])
+def test_request_sharding_is_exact_partition(world):
+    res = _run("requests", world)
     case = W.make_attention_case(78, [4000, 2500, 700, 5000, 3300])
     ref_out, ref_lse = O.dsa_attention(case.q_nope, case.q_pe, case.ckv, case.kpe, case.idx,
                                        case.sm_scale)
