@@ -33,7 +33,7 @@ class _Workspace:
         self.buf = None
         self.lock = threading.Lock()
 
-    def get(self, device, nbytes, vtokens, stream):
+    def get(self, device, nbytes):
         with self.lock:
             if self.buf is None or self.buf.numel() < nbytes:
                 self.buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
@@ -136,7 +136,7 @@ def _launch(fn, q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, nu
     with torch.cuda.device(device):
         stream = torch.cuda.current_stream(device)
         nbytes = _workspace_bytes(device, num_tokens, heads, topk)
-        ws = workspace_for(device).get(device, nbytes, num_tokens * (heads // NUM_HEADS), stream)
+        ws = workspace_for(device).get(device, nbytes)
         _lib.call(
             fn,
             q_nope.data_ptr(), q_nope.stride(0), q_nope.stride(1),
