@@ -38,11 +38,29 @@ def _alt_scale_case():
                                  sm_scale=0.1352337788608801)
 
 
+def _cfg2_small_case():
+    """cfg2's shape (T=64 tokens of independent requests, shuffled page
+    tables, 2048 distinct positions, -1 padded) with contexts drawn from
+    U[1024, 4096] instead of U[1024, 65536], so that the host can regenerate
+    the inputs in about a second."""
+    return W.make_attention_case(51, W.cfg2_ctx_lens(51, 64, 1024, 4096))
+
+
 CASES = {
     "cfg1_seed0": lambda: W.cfg1_case(0),
     "edge": _edge_case,
     "big_logits": _big_logits_case,
     "alt_scale": _alt_scale_case,
+    "cfg2_small": _cfg2_small_case,
+}
+
+# Indexer inputs for the reference's own indexer / top-k kernels: exact by
+# construction (every score exact in fp16 products and fp32 sums, in any
+# order), power-of-two batches, contexts short enough for the reference's
+# unrolled top-k loop.
+INDEXER_CASES = {
+    "exact_b4": lambda: W.make_indexer_case(61, [1024, 777, 1000, 512], exact=True),
+    "exact_b2": lambda: W.make_indexer_case(62, [1500, 333], exact=True),
 }
 
 
@@ -51,4 +69,11 @@ def digest(case: W.AttentionCase) -> str:
     for a in (case.q_nope, case.q_pe, case.ckv, case.kpe, case.idx):
         h.update(np.ascontiguousarray(a).tobytes())
     h.update(np.float32(case.sm_scale).tobytes())
+    return h.hexdigest()
+
+
+def indexer_digest(case: W.IndexerCase) -> str:
+    h = hashlib.sha256()
+    for a in (case.q, case.k, case.scale, case.w, case.block_table, case.seq_lens):
+        h.update(np.ascontiguousarray(a).tobytes())
     return h.hexdigest()
