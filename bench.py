@@ -302,12 +302,12 @@ def run_ours(args):
     clocks = clk.summary()
 
     # ---- the dominant kernel alone (roofline): the attention grid without the
-    # merge grid (DSA_ATTN_STAGE=1), captured and timed the same way
-    os.environ["DSA_ATTN_STAGE"] = "1"
-    with torch.cuda.stream(side):
-        op()
-    attn_ms = graph_timed_steps(op, min(args.steps, 200), flush, side, stream)
-    os.environ.pop("DSA_ATTN_STAGE")
+    # merge grid (profiling option attention_grids=1), captured and timed the same way
+    from flashinfer_repo_b200 import options
+    with options(attention_grids=1):
+        with torch.cuda.stream(side):
+            op()
+        attn_ms = graph_timed_steps(op, min(args.steps, 200), flush, side, stream)
     attn_kernel_ms = statistics.mean(attn_ms)
     kernel(qn, qp, ckv, kpe, idx, scale, output=out, lse=lse)  # leave complete results
 

@@ -5,6 +5,8 @@ sparse_indices, sm_scale) -> (output, lse)` (solution/triton/kernel.py:138-182)
 plus the FP8 lightning indexer and exact top-k that feed it.  All compute runs
 in libdsa_b200.so (hand-written CUDA for sm_100a, C ABI in include/dsa_b200.h).
 """
-from .kernel import kernel, kernel_splitk, kernel_splitk_v2, read_device_error  # noqa: F401
+from .kernel import (get_options, kernel, kernel_splitk, kernel_splitk_v2, options,  # noqa: F401
+                     read_device_error, set_options)
 
-__all__ = ["kernel", "kernel_splitk", "kernel_splitk_v2", "read_device_error"]
+__all__ = ["kernel", "kernel_splitk", "kernel_splitk_v2", "read_device_error", "options",
+           "set_options", "get_options"]

@@ -18,9 +18,19 @@ SZ = ctypes.c_size_t
 F32 = ctypes.c_float
 INT = ctypes.c_int
 
+class Options(ctypes.Structure):
+    """struct dsa_options (include/dsa_b200.h)."""
+    _fields_ = [("attention_kernel", ctypes.c_int), ("attention_stages", ctypes.c_int),
+                ("attention_ctas", ctypes.c_int), ("attention_min_tiles", ctypes.c_int),
+                ("attention_grids", ctypes.c_int), ("merge_pdl", ctypes.c_int),
+                ("indexer_tiles_per_cta", ctypes.c_int)]
+
+
 # name -> argtypes; every function returns int (dsa_status) except the message.
 SIGNATURES = {
     "dsa_sparse_attention_workspace_size": [I64, I64, I64, ctypes.POINTER(SZ)],
+    "dsa_set_options": [ctypes.POINTER(Options)],
+    "dsa_get_options": [ctypes.POINTER(Options)],
     "dsa_sparse_attention": [P, I64, I64, P, I64, I64, P, I64, I64, P, I64, I64, P, I64,
                              I64, I64, I64, I64, I64, F32, P, I64, I64, P, I64, I64, P, SZ, P],
     "dsa_sparse_attention_noalloc": [P, I64, I64, P, I64, I64, P, I64, I64, P, I64, I64, P, I64,

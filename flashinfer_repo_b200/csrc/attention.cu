@@ -921,13 +921,18 @@ struct DevInfo {
 std::mutex g_mu;
 DevInfo g_dev[64];
 
-int env_int(const char* name, int dflt) {
-  const char* s = getenv(name);
-  return (s && *s) ? atoi(s) : dflt;
+// Tuning / profiling options, process-wide, set only through dsa_set_options
+// (nothing is read from the environment).  Each call takes a copy.
+std::mutex g_opt_mu;
+dsa_options g_opt = {0, 0, 0, 0, 0, 1, 0};
+
+dsa_options current_options() {
+  std::lock_guard<std::mutex> lk(g_opt_mu);
+  return g_opt;
 }
 
-int stages_choice() {
-  const int s = env_int("DSA_ATTN_STAGES", 2);
+int stages_choice(const dsa_options& o) {
+  const int s = o.attention_stages ? o.attention_stages : 2;
   return (s >= 2 && s <= 4) ? s : 2;
 }
 
@@ -991,17 +996,18 @@ struct Plan {
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 // Grid plan: an even split of all tiles over min(slots, tiles/min_tiles) CTAs.
-// Which kernel: DSA_ATTN_IMPL=0 (default) the mma.sync kernel (32-row tiles),
-// 1 the tcgen05 kernel (64-row tiles).  With 16 heads every tcgen05 MMA has
-// N=16 and a 64-row tile in MMA layout takes 72 KB of shared memory (two
-// stages fit), so on this pool's B200 the tcgen05 kernel measured slower on
+// Which kernel: option attention_kernel 0 (default) or 1: the mma.sync kernel
+// (32-row tiles); 2: the tcgen05 kernel (64-row tiles).  With 16 heads every
+// tcgen05 MMA has N=16 and a 64-row tile in MMA layout takes 72 KB of shared
+// memory (two stages fit); measured on a B200 the tcgen05 kernel was slower on
 // both the HBM-bound decode (cfg2: 82 vs 53 us) and the L2-resident prefill
 // (cfg5: 3.2 vs 1.6 ms); it is kept as a tested alternative.
-int impl_choice() { return env_int("DSA_ATTN_IMPL", 0); }
+bool tc_choice(const dsa_options& o) { return o.attention_kernel == 2; }
 
 int tc_smem_bytes() { return (int)sizeof(TcSmem) + 1024; }
 
-int make_plan(int64_t num_tokens, int64_t heads, int64_t topk, int nst, Plan* pl, bool tc = false) {
+int make_plan(int64_t num_tokens, int64_t heads, int64_t topk, int nst, Plan* pl, bool tc,
+              const dsa_options& o) {
   int sms = 0;
   int occ = 0;
   if (tc) {
@@ -1013,11 +1019,9 @@ int make_plan(int64_t num_tokens, int64_t heads, int64_t topk, int nst, Plan* pl
   const int64_t tpt = topk / (tc ? kTcRows : kRows);
   pl->vtokens = num_tokens * (heads / kHeads);
   pl->total_tiles = pl->vtokens * tpt;
-  const int mt_env = env_int("DSA_ATTN_MIN_TILES", tc ? 2 : 4);
-  const int min_tiles = mt_env > 0 ? mt_env : 1;
+  const int min_tiles = o.attention_min_tiles > 0 ? o.attention_min_tiles : (tc ? 2 : 4);
   int64_t ctas = (int64_t)sms * occ;
-  const int forced = env_int("DSA_ATTN_CTAS", 0);
-  if (forced > 0) ctas = forced;
+  if (o.attention_ctas > 0) ctas = o.attention_ctas;
   ctas = std::min<int64_t>(ctas, (pl->total_tiles + min_tiles - 1) / min_tiles);
   if (ctas < 1) ctas = 1;
   pl->ctas = (int)ctas;
@@ -1086,14 +1090,15 @@ static int attention_impl(const void* q_nope, int64_t q_nope_stride_token, int64
     return fail(DSA_ERR_INVALID_ARG, "q rows must be 4-byte aligned");
   if ((reinterpret_cast<uintptr_t>(output) & 7) || out_stride_token % 4 || out_stride_head % 4)
     return fail(DSA_ERR_INVALID_ARG, "output rows must be 8-byte aligned");
-  const int nst = stages_choice();
+  const dsa_options opt = current_options();
+  const int nst = stages_choice(opt);
   // the tcgen05 kernel gathers queries with 16-byte copies
   const bool q16 = !(reinterpret_cast<uintptr_t>(q_nope) & 15) && !(reinterpret_cast<uintptr_t>(q_pe) & 15) &&
                    q_nope_stride_token % 8 == 0 && q_nope_stride_head % 8 == 0 &&
                    q_pe_stride_token % 8 == 0 && q_pe_stride_head % 8 == 0;
-  const bool tc = impl_choice() == 1 && topk % kTcRows == 0 && q16;
+  const bool tc = tc_choice(opt) && topk % kTcRows == 0 && q16;
   Plan pl;
-  int rc = make_plan(num_tokens, num_heads, topk, nst, &pl, tc);
+  int rc = make_plan(num_tokens, num_heads, topk, nst, &pl, tc, opt);
   if (rc) return rc;
   if (workspace_bytes < pl.bytes || (reinterpret_cast<uintptr_t>(workspace) & 255))
     return fail(DSA_ERR_WORKSPACE, "workspace too small or not 256-byte aligned");
@@ -1135,9 +1140,9 @@ static int attention_impl(const void* q_nope, int64_t q_nope_stride_token, int64
   p.part = reinterpret_cast<float*>(ws + pl.part_off);
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // Profiling knob DSA_ATTN_STAGE: 1 = attention grid only, 2 = merge grid
-  // only (on the partials of an earlier call with the same shapes); default both.
-  const int stage = env_int("DSA_ATTN_STAGE", 0);
+  // Profiling option attention_grids: 1 = attention grid only, 2 = merge grid
+  // only (on the partials of an earlier call with the same shapes); 0 both.
+  const int stage = opt.attention_grids;
   cudaError_t e = cudaSuccess;
   if (stage != 2) {
     if (tc) {
@@ -1163,7 +1168,7 @@ static int attention_impl(const void* q_nope, int64_t q_nope_stride_token, int64
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = env_int("DSA_ATTN_PDL", 1) ? 1 : 0;
+    cfg.numAttrs = opt.merge_pdl ? 1 : 0;
     e = cudaLaunchKernelEx(&cfg, dsa_attention_merge_kernel, p);
     if (e != cudaSuccess) return fail(DSA_ERR_CUDA, cudaGetErrorString(e));
   }
@@ -1180,10 +1185,40 @@ int dsa_sparse_attention_workspace_size(int64_t num_tokens, int64_t num_heads, i
   if (num_tokens < 0 || num_heads <= 0 || num_heads % kHeads || topk <= 0 || topk % kRows)
     return fail(DSA_ERR_INVALID_ARG, "num_heads must be a multiple of 16 and topk of 32");
   Plan pl;
-  const bool tc = impl_choice() == 1 && topk % kTcRows == 0;
-  const int rc = make_plan(num_tokens > 0 ? num_tokens : 1, num_heads, topk, stages_choice(), &pl, tc);
+  const dsa_options opt = current_options();
+  // q alignment is unknown here: size for the larger of the two plans
+  Plan pl_tc;
+  int rc = make_plan(num_tokens > 0 ? num_tokens : 1, num_heads, topk, stages_choice(opt), &pl, false,
+                     opt);
   if (rc) return rc;
+  if (tc_choice(opt) && topk % kTcRows == 0) {
+    rc = make_plan(num_tokens > 0 ? num_tokens : 1, num_heads, topk, stages_choice(opt), &pl_tc, true,
+                   opt);
+    if (rc) return rc;
+    if (pl_tc.bytes > pl.bytes) pl = pl_tc;
+  }
   *bytes = pl.bytes;
+  return DSA_OK;
+}
+
+int dsa_set_options(const dsa_options* options) {
+  dsa_options o = {0, 0, 0, 0, 0, 1, 0};
+  if (options) {
+    o = *options;
+    if (o.attention_kernel < 0 || o.attention_kernel > 2 || o.attention_stages < 0 ||
+        o.attention_stages > 4 || o.attention_stages == 1 || o.attention_ctas < 0 ||
+        o.attention_min_tiles < 0 || o.attention_grids < 0 || o.attention_grids > 2 ||
+        o.merge_pdl < 0 || o.merge_pdl > 1 || o.indexer_tiles_per_cta < 0)
+      return fail(DSA_ERR_INVALID_ARG, "dsa_set_options: a field is out of range");
+  }
+  std::lock_guard<std::mutex> lk(g_opt_mu);
+  g_opt = o;
+  return DSA_OK;
+}
+
+int dsa_get_options(dsa_options* options) {
+  if (!options) return fail(DSA_ERR_INVALID_ARG, "options is NULL");
+  *options = current_options();
   return DSA_OK;
 }
 

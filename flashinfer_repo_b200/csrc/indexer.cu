@@ -222,10 +222,6 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-int env_int_idx(const char* name, int dflt) {
-  const char* s = getenv(name);
-  return (s && *s) ? atoi(s) : dflt;
-}
 
 }  // namespace
 }  // namespace dsa
@@ -286,7 +282,9 @@ extern "C" int dsa_indexer_scores(const void* q_fp8, const void* k_cache_fp8, in
   p.scores = scores;
   p.scores_stride = scores_stride;
   p.num_pages = num_pages;
-  p.tiles_per_cta = env_int_idx("DSA_INDEXER_TILES_PER_CTA", 16);
+  dsa_options opt;
+  dsa_get_options(&opt);
+  p.tiles_per_cta = opt.indexer_tiles_per_cta > 0 ? opt.indexer_tiles_per_cta : 16;
   if (p.tiles_per_cta < 1) p.tiles_per_cta = 1;
   p.err = device_error;
   const int smem = (int)sizeof(IdxSmem) + 1024;

@@ -10,8 +10,8 @@ tensors or a missing library raise.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
-import os
 import threading
 
 import torch
@@ -109,11 +109,46 @@ def kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, *, outp
     return output, lse
 
 
+_OPTION_FIELDS = [f for f, _ in _lib.Options._fields_]
+_options_generation = [0]  # bumped by set_options: cached workspace sizes depend on the plan
+
+
+def get_options() -> dict:
+    """The library's current tuning options (struct dsa_options) as a dict."""
+    o = _lib.Options()
+    _lib.call("dsa_get_options", ctypes.byref(o))
+    return {f: getattr(o, f) for f in _OPTION_FIELDS}
+
+
+def set_options(**fields) -> None:
+    """Set tuning/profiling options of the native library (process-wide).
+    Unnamed fields keep their defaults; set_options() restores all defaults.
+    Nothing is read from the environment."""
+    unknown = set(fields) - set(_OPTION_FIELDS)
+    if unknown:
+        raise TypeError(f"unknown option(s) {sorted(unknown)}")
+    o = _lib.Options(merge_pdl=1)
+    for f, v in fields.items():
+        setattr(o, f, int(v))
+    _lib.call("dsa_set_options", ctypes.byref(o))
+    _options_generation[0] += 1
+
+
+@contextlib.contextmanager
+def options(**fields):
+    """`with options(attention_ctas=7): ...` -- options for the block, the
+    previous set restored afterwards (for tests and profiling)."""
+    prev = get_options()
+    set_options(**fields)
+    try:
+        yield
+    finally:
+        set_options(**prev)
+
+
 def _workspace_bytes(device, num_tokens, heads, topk):
-    # the plan (and so the size) also depends on the tuning knobs
-    key = (device.index, num_tokens, heads, topk, os.environ.get("DSA_ATTN_CTAS"),
-           os.environ.get("DSA_ATTN_MIN_TILES"), os.environ.get("DSA_ATTN_STAGES"),
-           os.environ.get("DSA_ATTN_IMPL"))
+    # the plan (and so the size) also depends on the tuning options
+    key = (device.index, num_tokens, heads, topk, _options_generation[0])
     nbytes = _ws_size_cache.get(key)
     if nbytes is None:
         n = ctypes.c_size_t(0)

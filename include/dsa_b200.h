@@ -50,9 +50,40 @@ enum dsa_device_error {
 const char* dsa_last_error_message(void);
 
 /*
+ * Tuning and profiling options, process-wide (no counterpart in the
+ * reference, whose kernels take their block sizes as Triton constexprs).
+ * The library reads no environment variable; these values are the only way
+ * to change a launch plan.  Zero selects the default of a field.
+ *   attention_kernel   0 default; 1 the mma.sync kernel (32-row tiles);
+ *                      2 the tcgen05 kernel (64-row tiles, TMEM accumulators)
+ *   attention_stages   shared-memory ring depth of the mma.sync kernel, 2..4
+ *   attention_ctas     grid size (0: resident CTAs per SM x SMs)
+ *   attention_min_tiles  fewest 32-row tiles per CTA (0: 4)
+ *   attention_grids    PROFILING ONLY: 1 launches the attention grid alone
+ *                      (outputs of tokens split across CTAs are then not
+ *                      written), 2 the merge grid alone; 0 both
+ *   merge_pdl          1 (default) launches the merge grid as a programmatic
+ *                      dependent of the attention grid; 0 a plain launch
+ *   indexer_tiles_per_cta  128-token tiles per indexer CTA (0: 16)
+ * dsa_set_options(NULL) restores every default.  Changing options while
+ * other host threads launch gives each launch either the old or the new set.
+ */
+typedef struct dsa_options {
+  int attention_kernel;
+  int attention_stages;
+  int attention_ctas;
+  int attention_min_tiles;
+  int attention_grids;
+  int merge_pdl;
+  int indexer_tiles_per_cta;
+} dsa_options;
+int dsa_set_options(const dsa_options* options);
+int dsa_get_options(dsa_options* options);
+
+/*
  * Workspace bytes dsa_sparse_attention needs for this shape on the current
- * device.  The workspace holds a device error word, one arrival counter per
- * (token, 16-head group) and the split-K partial results.
+ * device.  Layout: the device error word (first 256 bytes), then two split-K
+ * partial slots per CTA of the launch plan (acc[16][512], m[16], l[16] fp32).
  */
 int dsa_sparse_attention_workspace_size(int64_t num_tokens, int64_t num_heads, int64_t topk,
                                         size_t* bytes);

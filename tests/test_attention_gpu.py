@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 import torch
 
-from flashinfer_repo_b200 import kernel, read_device_error
+from flashinfer_repo_b200 import kernel, options, read_device_error
 from flashinfer_repo_b200 import workloads as W
 from oracle import oracle as O
 from tests.golden.cases import CASES, digest
@@ -20,10 +20,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 
 @pytest.fixture(autouse=True)
-def _env_guard(monkeypatch):
-    for k in ("DSA_ATTN_CTAS", "DSA_ATTN_STAGES", "DSA_ATTN_MIN_TILES", "DSA_ATTN_IMPL"):
-        monkeypatch.delenv(k, raising=False)
-    yield
+def _default_options():
+    with options():
+        yield
 
 
 @pytest.mark.parametrize("name", list(CASES))
@@ -53,21 +52,33 @@ def test_batched_ragged_contexts(cuda_device, seed):
     _oracle_check(case, cuda_device)
 
 
-@pytest.mark.parametrize("ctas", ["1", "3", "7", "64", "500"])
-def test_split_counts_agree(cuda_device, monkeypatch, ctas):
+@pytest.mark.parametrize("ctas", [1, 3, 7, 64, 500])
+def test_split_counts_agree(cuda_device, ctas):
     """Any partition of the top-k dimension over CTAs gives the oracle's answer
     (split-K equivalence, cf. test_splitk_correctness.py:20-26)."""
-    monkeypatch.setenv("DSA_ATTN_CTAS", ctas)
-    monkeypatch.setenv("DSA_ATTN_MIN_TILES", "1")
     case = W.make_attention_case(7, [5000, 3000, 1500, 4096, 2048])
-    _oracle_check(case, cuda_device)
+    with options(attention_ctas=ctas, attention_min_tiles=1):
+        _oracle_check(case, cuda_device)
 
 
-@pytest.mark.parametrize("stages", ["2", "3", "4"])
-def test_pipeline_depths(cuda_device, monkeypatch, stages):
-    monkeypatch.setenv("DSA_ATTN_STAGES", stages)
+@pytest.mark.parametrize("stages", [2, 3, 4])
+def test_pipeline_depths(cuda_device, stages):
     case = W.make_attention_case(8, [5000, 2100, 4096])
-    _oracle_check(case, cuda_device)
+    with options(attention_stages=stages):
+        _oracle_check(case, cuda_device)
+
+
+def test_environment_is_not_read(cuda_device, monkeypatch):
+    """Leftover variables of the old profiling knobs change nothing: a stray
+    DSA_ATTN_STAGE=2 once made kernel() run the merge grid alone."""
+    case = W.make_attention_case(16, [5000, 3000, 4096])
+    args = case_to_device(case, cuda_device)
+    ref_out, ref_lse = kernel(*args, case.sm_scale)
+    for k, v in (("DSA_ATTN_STAGE", "2"), ("DSA_ATTN_IMPL", "1"), ("DSA_ATTN_CTAS", "3"),
+                 ("DSA_ATTN_PDL", "0"), ("DSA_ATTN_STAGES", "4"), ("DSA_ATTN_MIN_TILES", "1")):
+        monkeypatch.setenv(k, v)
+    out, lse = kernel(*args, case.sm_scale)
+    assert torch.equal(out, ref_out) and torch.equal(lse, ref_lse)
 
 
 def test_deterministic(cuda_device):
@@ -172,22 +183,20 @@ def test_tvm_ffi_entry_point(cuda_device):
 
 
 @pytest.mark.parametrize("name", list(CASES))
-def test_tcgen05_variant_golden(cuda_device, monkeypatch, name):
+def test_tcgen05_variant_golden(cuda_device, name):
     """The tcgen05 kernel (64-row tiles, TMEM accumulators) on the reference's
     golden outputs."""
-    monkeypatch.setenv("DSA_ATTN_IMPL", "1")
     case = CASES[name]()
     g = np.load(os.path.join(HERE, "golden", f"attn_{name}.npz"))
-    out, lse = kernel(*case_to_device(case, cuda_device), case.sm_scale)
+    with options(attention_kernel=2):
+        out, lse = kernel(*case_to_device(case, cuda_device), case.sm_scale)
     assert_attention_close(out, lse, g["out"], g["lse"], name)
 
 
-@pytest.mark.parametrize("ctas", ["1", "5", "64"])
-def test_tcgen05_variant_ragged_and_splits(cuda_device, monkeypatch, ctas):
-    monkeypatch.setenv("DSA_ATTN_IMPL", "1")
-    monkeypatch.setenv("DSA_ATTN_CTAS", ctas)
-    monkeypatch.setenv("DSA_ATTN_MIN_TILES", "1")
+@pytest.mark.parametrize("ctas", [1, 5, 64])
+def test_tcgen05_variant_ragged_and_splits(cuda_device, ctas):
     case = W.make_attention_case(15, [5000, 300, 3000, 64, 9000, 2048])
     case.idx[2, 100:900] = -1
     case.idx[3, :] = -1
-    _oracle_check(case, cuda_device)
+    with options(attention_kernel=2, attention_ctas=ctas, attention_min_tiles=1):
+        _oracle_check(case, cuda_device)
