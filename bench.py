@@ -14,14 +14,26 @@ achieved HBM GB/s of the attention kernel against MEASURED_PEAKS.json.
 L2 is flushed (256 MiB write, then a 256 MiB read) before every timed step; each step is timed
 with CUDA events on the launching stream and summed, max over ranks.
 
---impl reference times the reference algorithm on the host cores instead:
-the CPU port of the reference golden function (oracle/, the reference
-itself is Python and cannot be installed on the GPU box), rank 0 only.
+--impl reference times the reference's own CPU implementation of the path
+on the host cores instead: its golden PyTorch function `run`
+(solution/triton/indexer_kernel.py:436-497), imported unmodified from the
+copy in baseline/_ref (placed there by baseline/install_reference.py), on the
+same cfg2 batch with all host threads; rank 0 only (the number is one host's,
+not per GPU).  Without baseline/_ref the CPU port of `run` in oracle/ is timed
+instead and the line says so.
+
+The default line also carries a "cfg4" object (indexer + top-k + attention
+step of BASELINE cfg4 on this GPU) and, under torchrun with N >= 2, a "cfg3"
+object (128 heads sharded over the N GPUs, gather fused into the epilogues,
+with the NCCL all-gather variant and a parity flag against a local 128-head
+computation).
 """
 from __future__ import annotations
 
 import argparse
+import importlib.util
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -193,6 +205,55 @@ def dist_setup(n):
     return rank, world, local
 
 
+def reference_run_fn():
+    """The reference golden function `run` (solution/triton/indexer_kernel.py:
+    436-497) from the unmodified copy in baseline/_ref, or (None, reason).
+    The module uses `math` without importing it (:490), so `math` is added to
+    its namespace; its file is not changed."""
+    path = os.path.join(ROOT, "baseline", "_ref", "solution", "triton", "indexer_kernel.py")
+    if not os.path.isfile(path):
+        return None, "baseline/_ref is missing (baseline/install_reference.py was not run)"
+    try:
+        spec = importlib.util.spec_from_file_location("_ref_indexer_kernel", path)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+    except Exception as e:  # noqa: BLE001  (e.g. triton missing on the host)
+        return None, f"cannot import the reference: {type(e).__name__}: {e}"
+    mod.math = math
+    return mod.run, None
+
+
+def reference_cpu_run(qn, qp, ckv, kpe, idx, scale, max_calls, budget_s=60.0, warmup=1):
+    """Time the reference `run` on the host cores (torch CPU, all threads) on
+    the full batch: one call = every token of the batch over the whole cache,
+    which `run` first upcasts to fp32 (indexer_kernel.py:458-459), exactly as
+    the reference evaluates it.  Times up to max_calls calls, stopping once
+    budget_s is spent (at least one).  Returns None when the reference is not
+    available, else a dict (tokens/s, cores, sample, calls)."""
+    run, why = reference_run_fn()
+    if run is None:
+        return {"unavailable": why}
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    h = [t.detach().cpu() for t in (qn, qp, ckv, kpe, idx)]
+    for _ in range(warmup):
+        run(*h, scale)
+    times, t_all = [], time.perf_counter()
+    while len(times) < max(1, max_calls):
+        t0 = time.perf_counter()
+        run(*h, scale)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_all > budget_s:
+            break
+    T = idx.shape[0]
+    med = statistics.median(times)
+    return {"value": T / med, "unit": UNIT, "cores": cores, "kind": "reference",
+            "sample": f"reference run() (baseline/_ref, torch CPU, {torch.get_num_threads()} threads) "
+                      f"on the full batch of {T} tokens and its whole cache, median of "
+                      f"{len(times)} call(s) after {warmup} warm-up",
+            "calls": len(times), "s_per_call": med}
+
+
 def cpu_baseline_run(qn, qp, ckv, kpe, idx, scale, reps=3):
     """The reference algorithm (CPU port in oracle/) on the rows of the same
     batch: the selected rows are compacted into a small host cache so the
@@ -232,25 +293,62 @@ def run_reference_arm(args):
     from flashinfer_repo_b200.bench_inputs import make_cfg2_device
     dev = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
     qn, qp, ckv, kpe, idx, scale = make_cfg2_device(seed=0, device=dev)
-    vals = []
-    for i in range(args.warmup + args.steps):
-        v, cores, sample = cpu_baseline_run(qn, qp, ckv, kpe, idx, scale, reps=1)
-        if i >= args.warmup:
-            vals.append(v)
-    v = statistics.median(vals)
+    T = int(idx.shape[0])
+    ref = reference_cpu_run(qn, qp, ckv, kpe, idx, scale, max_calls=args.steps, budget_s=90.0,
+                            warmup=min(args.warmup, 1))
+    if "unavailable" not in ref:
+        v, cb, dtype = ref["value"], ref, "f32"
+        steps = ref["calls"]
+        note = ("reference arm: the reference's own golden CPU function run() "
+                "(solution/triton/indexer_kernel.py:436-497), unmodified, from baseline/_ref, "
+                "on all host threads; one step = one run() call on the whole batch; timed calls "
+                "capped by a 90 s budget (steps = calls actually timed)")
+    else:  # no reference copy on this machine: the CPU port of run()
+        vals = []
+        for i in range(args.warmup + min(args.steps, 10)):
+            v, cores, sample = cpu_baseline_run(qn, qp, ckv, kpe, idx, scale, reps=1)
+            if i >= args.warmup:
+                vals.append(v)
+        v = statistics.median(vals)
+        steps, dtype = len(vals), "f64"
+        cb = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+        note = f"reference arm: {ref['unavailable']}; timed the CPU port of run() (oracle/) instead"
+    cb = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * idx.shape[0] / v,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "steps": steps, "steps_requested": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * T / v,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype,
         "data": "synthetic (seeded, BASELINE cfg2 shapes and distributions)",
-        "config": {"workload": WORKLOAD, "tokens_per_gpu": int(idx.shape[0]),
-                   "note": "reference arm: CPU port of the reference golden function "
-                           "(solution/triton/indexer_kernel.py:436-497) on all host cores; the "
-                           "reference has no installable package"},
-        "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": sample},
+        "config": {"workload": WORKLOAD, "tokens_per_gpu": T,
+                   "parallelism": f"request-shard x{args.gpus} (reference arm: rank 0's host only)",
+                   "l2": "not applicable (host CPU)", "launch": "host CPU, torch",
+                   "note": note},
+        "cpu_baseline": cb,
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
+
+
+def copy_bandwidth(dev, nbytes=64 << 20, reps=5):
+    """Pinned host<->device copy bandwidth (GB/s) of this machine, measured
+    with CUDA events: the context for the e2e number."""
+    h = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    d = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    out = {}
+    for name, fn in (("h2d_gbs", lambda: d.copy_(h, non_blocking=True)),
+                     ("d2h_gbs", lambda: h.copy_(d, non_blocking=True))):
+        fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            ts.append(a.elapsed_time(b))
+        out[name] = nbytes / (min(ts) / 1e3) / 1e9
+    return out
 
 
 def run_ours(args):
@@ -478,11 +576,22 @@ def run_ours(args):
     achieved = alg_bytes / (avg_kernel_ms / 1e3) / 1e9
     peak, peak_kind = peaks()
 
+    copies = copy_bandwidth(dev)
+    cfg4 = measure_cfg4(dev, rank, min(args.steps, 20), args.warmup, 128)
+    cfg3 = measure_cfg3(dev, world, rank, min(args.steps, 20), args.warmup, dist) if world > 1 else None
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         os.sched_setaffinity(0, all_cpus)  # the CPU baseline uses every host core
+        ref = reference_cpu_run(qn, qp, ckv, kpe, idx, scale, max_calls=3, budget_s=30.0)
         v, cores, sample = cpu_baseline_run(qn, qp, ckv, kpe, idx, scale)
-        cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+        port = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample,
+                "note": "the fp64 C port of run() in oracle/, selected rows compacted"}
+        if "unavailable" in ref:
+            cpu = dict(port, note=port["note"] + "; reference unavailable: " + ref["unavailable"])
+        else:
+            cpu = {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            cpu["port"] = port
 
     if rank == 0:
         print(json.dumps({
@@ -496,7 +605,7 @@ def run_ours(args):
                        "alg_bytes_per_step_per_gpu": alg_bytes},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": ATTN_TRAFFIC_PER_LAUNCH,
-                         "traffic_unit": "bytes per launch (ncu dram read+write, profiles/dsa_attention_kernel_cfg2.md)",
+                         "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
                          "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
                          "kernel": "dsa_attention_kernel", "avg_kernel_ms": avg_kernel_ms,
                          "step_ms_incl_merge_grid": statistics.mean(step_ms),
@@ -507,39 +616,40 @@ def run_ours(args):
                     "host_numa": numa,
                     "host_driven_ms_per_step": e2e_a / args.steps,
                     "one_graph_ms_per_step": e2e_b / args.steps,
-                    "pcie_floor_ms_per_step": h2d / 55e9 * 1e3,
+                    "pcie_floor_ms_per_step": h2d / (copies["h2d_gbs"] * 1e9) * 1e3,
+                    "copy_bandwidth_gbs": copies,
                     "note": "kernel() with pinned host buffers: per step the upload of q_nope, "
                             "q_pe and sparse_indices (one staging buffer, one copy), the operator, "
                             "and the download of output + "
                             "LSE, pipelined over upload/compute/download streams (4 buffer sets), driven "
                             "by the host per step or as 40 steps in one multi-stream CUDA graph (the "
                             "faster is the value), alternating two batches (inputs "
-                            "larger than L2); pcie_floor = upload bytes at the 55 GB/s measured "
-                            "for pinned copies on this host"},
+                            "larger than L2); pcie_floor = upload bytes at the pinned host-to-device "
+                            "bandwidth measured on this machine (copy_bandwidth_gbs)"},
             "gpu_launches": 2 * args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,
+            "cfg4": cfg4,
+            "cfg3": cfg3,
         }), flush=True)
     if dist:
         dist.destroy_process_group()
 
 
-def run_cfg4(args):
-    """BASELINE cfg4: one DSA decode step = FP8 indexer over 128 requests x
-    32768 tokens -> exact top-2048 -> 16-head sparse MLA attention on the
-    selected slots.  Reports per-kernel device time and the indexer roofline."""
-    rank, world, local = dist_setup(args.gpus)
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
+def measure_cfg4(dev, rank, steps, warmup, requests):
+    """BASELINE cfg4 on this GPU: one DSA decode step = FP8 indexer over
+    `requests` requests x 32768 tokens -> exact top-2048 -> 16-head sparse MLA
+    attention on the selected slots.  Each stage is one CUDA graph; the three
+    replays of a step run behind an untimed L2 flush and a GPU sleep, so the
+    events see device time only.  Returns per-stage times and rooflines."""
     from flashinfer_repo_b200 import indexer as IX
     from flashinfer_repo_b200 import kernel
     from flashinfer_repo_b200.bench_inputs import attention_bytes, indexer_bytes, make_cfg4_device
-    d = make_cfg4_device(seed=2000 + rank, device=dev, T=args.requests)
+    d = make_cfg4_device(seed=2000 + rank, device=dev, T=requests)
     T = d["seq_lens"].numel()
     flush = L2Flush(dev)
     stream = torch.cuda.current_stream(dev)
     scores = torch.empty((T, d["block_table"].shape[1] * 64), dtype=torch.float32, device=dev)
-
     out = torch.empty((T, 16, 512), dtype=torch.bfloat16, device=dev)
     lse = torch.empty((T, 16), dtype=torch.float32, device=dev)
     box = {}
@@ -552,8 +662,6 @@ def run_cfg4(args):
 
     def k_attention():
         kernel(d["q_nope"], d["q_pe"], d["ckv"], d["kpe"], box["slots"], d["sm_scale"], output=out, lse=lse)
-    # each stage captured once in a CUDA graph; the three replays of a step are
-    # queued behind a GPU sleep, so the events see device time only
     side = torch.cuda.Stream(dev)
     side.wait_stream(stream)
     graphs = []
@@ -568,14 +676,14 @@ def run_cfg4(args):
             graphs.append(g)
     stream.wait_stream(side)
     slots = box["slots"]
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         flush(1)
         for g in graphs:
             g.replay()
     torch.cuda.synchronize()
     parts = np.zeros(3)
-    with ClockSampler(local) as clk:
-        for i in range(args.steps):
+    with ClockSampler(dev.index) as clk:
+        for i in range(steps):
             flush(i)
             torch.cuda._sleep(100_000)
             ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
@@ -585,64 +693,93 @@ def run_cfg4(args):
                 ev[j + 1].record(stream)
             ev[3].synchronize()
             parts += [ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]), ev[2].elapsed_time(ev[3])]
-    parts /= args.steps
+    parts /= steps
     total = parts.sum()
     ib = indexer_bytes(d["seq_lens"])
+    ab = attention_bytes(slots)
     peak, kind = peaks()
-    print(json.dumps({
-        "metric": "DSA decode step (indexer + top-k + attention) query-tokens/sec", "value": T / (total / 1e3),
-        "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": total,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp8+bf16",
-        "data": "synthetic (seeded, BASELINE cfg4 shapes and distributions)",
-        "config": {"workload": "cfg4: T=128 requests, ctx 32768, FP8 indexer 64x128, top-2048, 16-head MLA",
-                   "l2": L2_NOTE},
+    res = {
+        "workload": f"cfg4: T={T} requests, ctx 32768, FP8 indexer 64x128, top-2048, 16-head MLA",
+        "steps": steps, "value": T / (total / 1e3), "unit": UNIT, "ms_per_step": total,
         "kernels_ms": {"indexer": parts[0], "topk": parts[1], "attention": parts[2]},
-        "roofline": {"bound": "hbm", "kernel": "dsa_indexer_kernel", "achieved": ib / (parts[0] / 1e3) / 1e9,
-                     "peak": peak, "unit": "GB/s", "frac": ib / (parts[0] / 1e3) / 1e9 / peak,
-                     "traffic": None, "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({kind})"},
-        "attention_roofline": {"achieved": attention_bytes(slots) / (parts[2] / 1e3) / 1e9, "unit": "GB/s"},
-        "gpu_launches": 4 * args.steps,  # indexer, top-k, attention, merge
+        "indexer_roofline": {"bound": "hbm", "kernel": "dsa_indexer_kernel", "alg_bytes": ib,
+                             "achieved": ib / (parts[0] / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                             "frac": ib / (parts[0] / 1e3) / 1e9 / peak,
+                             "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({kind})"},
+        "attention_roofline": {"alg_bytes": ab, "achieved": ab / (parts[2] / 1e3) / 1e9, "unit": "GB/s",
+                               "frac": ab / (parts[2] / 1e3) / 1e9 / peak},
+        "gpu_launches_per_step": 4,  # indexer, top-k, attention, merge
         "clocks": clk.summary(),
-    }), flush=True)
+    }
+    del d, scores, out, lse, box, graphs
+    torch.cuda.empty_cache()
+    return res
 
 
-def run_cfg3(args):
-    """BASELINE cfg3: T=8 tokens, 128 heads, context 131072, clustered top-k,
-    latent cache replicated on every GPU; heads sharded 128/N per rank, each
-    rank's epilogues storing its heads into every rank's output over NVLink
-    (peer barrier after); the NCCL all-gather variant is timed beside it.  Strong scaling: the job is fixed."""
+def run_cfg4(args):
+    """BASELINE cfg4 alone (see measure_cfg4)."""
     rank, world, local = dist_setup(args.gpus)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    import torch.distributed as dist
+    r = measure_cfg4(dev, rank, args.steps, args.warmup, args.requests)
+    print(json.dumps({
+        "metric": "DSA decode step (indexer + top-k + attention) query-tokens/sec", "value": r["value"],
+        "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp8+bf16", "data": "synthetic (seeded, BASELINE cfg4 shapes and distributions)",
+        "config": {"workload": r["workload"], "l2": L2_NOTE},
+        "kernels_ms": r["kernels_ms"],
+        "roofline": dict(r["indexer_roofline"], traffic=None),
+        "attention_roofline": r["attention_roofline"],
+        "gpu_launches": 4 * args.steps, "clocks": r["clocks"],
+    }), flush=True)
+
+
+def measure_cfg3(dev, world, rank, steps, warmup, dist):
+    """BASELINE cfg3 over the `world` GPUs of this job: T=8 tokens, 128 heads,
+    context 131072, clustered top-k, latent cache replicated on every GPU;
+    heads sharded 128/N per rank.  Timed, max over ranks: the fused step (each
+    rank's epilogues store its heads into every rank's output over NVLink, then
+    the peer barrier), the NCCL all-gather step (16k-head kernel, pack,
+    all_gather_into_tensor, unpack) and the per-rank kernel alone.  Parity:
+    both gathered results are compared with a 128-head computation on this GPU
+    (same inputs), flags ANDed over ranks."""
     from flashinfer_repo_b200 import kernel
     from flashinfer_repo_b200.bench_inputs import attention_bytes, make_cfg3_device
     from flashinfer_repo_b200.parallel import PeerHeadShardedAttention, head_sharded_attention
-    if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
     qn, qp, ckv, kpe, idx, scale = make_cfg3_device(seed=3000, device=dev)  # same on every rank
     T, H = qn.shape[:2]
     h = H // world
     sl = slice(h * rank, h * (rank + 1))
     stream = torch.cuda.current_stream(dev)
     flush = L2Flush(dev)
-
     peer = PeerHeadShardedAttention(T, H, dev) if world > 1 else None
 
-    def step():  # fused: epilogues store into every rank's output, one peer barrier
+    def step():
         if world > 1:
             return peer(qn, qp, ckv, kpe, idx, scale)
         return kernel(qn, qp, ckv, kpe, idx, scale)
 
-    def step_allgather():  # unfused: 16-head kernel, pack, NCCL all-gather, unpack
+    def step_allgather():
         return head_sharded_attention(qn, qp, ckv, kpe, idx, scale)
-    for _ in range(args.warmup):
+    # parity first (fresh results of both paths against the local 128-head call)
+    full_out, full_lse = kernel(qn, qp, ckv, kpe, idx, scale)
+    fo, fl = step()
+    go, gl = step_allgather()
+    torch.cuda.synchronize()
+    parity = torch.tensor([
+        int(torch.equal(fo, full_out) and torch.equal(fl, full_lse)),
+        int(torch.equal(go, full_out) and torch.equal(gl, full_lse))], dtype=torch.int64, device=dev)
+    maxdiff = torch.tensor([(fo.float() - full_out.float()).abs().max().item(),
+                            (go.float() - full_out.float()).abs().max().item()],
+                           dtype=torch.float64, device=dev)
+    for _ in range(warmup):
         step()
         if world > 1:
             step_allgather()
     torch.cuda.synchronize()
     k_ms, s_ms, g_ms = [], [], []
-    for i in range(args.steps):
+    for i in range(steps):
         if world > 1:  # the all-gather variant, for comparison (same L2 state)
             flush(i)
             dist.barrier()
@@ -676,32 +813,54 @@ def run_cfg3(args):
                       statistics.median(g_ms) if g_ms else 0.0], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    kms, sms, gms = t.tolist()
-    peak, kind = peaks()
-    if rank == 0:
-        ab = attention_bytes(idx) * (h // 16)  # the 16-head operator's bytes per head group
-        print(json.dumps({
-            "metric": "DSA decode query-tokens/sec, 128 heads (head-sharded)", "value": T / (sms / 1e3),
-            "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": sms,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded, BASELINE cfg3 shapes and distributions)",
-            "config": {"workload": "cfg3: T=8, 128 heads, ctx 131072, clustered top-2048",
-                       "parallelism": f"heads {h}/rank x {world}" + (
-                           ", outputs stored into every rank's buffer by the epilogues + peer barrier"
-                           if world > 1 else ""),
-                       "l2": L2_NOTE},
-            "kernel_ms": kms, "step_ms_fused_gather": sms,
-            "step_ms_nccl_allgather": gms if world > 1 else None,
-            "roofline": {"bound": "hbm", "kernel": "dsa_attention_kernel",
-                         "achieved": ab / (kms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
-                         "frac": ab / (kms / 1e3) / 1e9 / peak, "traffic": None,
-                         "note": "algorithmic bytes per rank = 16-head operator bytes x head groups "
-                                 "(repeat row reads of the groups are served from L2)"},
-            "gpu_launches": args.steps * (3 if world > 1 else 2),  # attention + merge (+ peer barrier)
-        }), flush=True)
-    if world > 1:
+        dist.all_reduce(parity, op=dist.ReduceOp.MIN)
+        dist.all_reduce(maxdiff, op=dist.ReduceOp.MAX)
         dist.barrier()
         peer.close()
+    kms, sms, gms = t.tolist()
+    peak, _ = peaks()
+    ab = attention_bytes(idx) * (h // 16)  # the 16-head operator's bytes per head group
+    return {
+        "workload": "cfg3: T=8, 128 heads, ctx 131072, clustered top-2048",
+        "parallelism": f"heads {h}/rank x {world}" + (
+            ", outputs stored into every rank's buffer by the epilogues + peer barrier" if world > 1 else ""),
+        "scaling": "strong", "steps": steps,
+        "value": T / (sms / 1e3), "unit": UNIT,
+        "ms_per_step_fused_gather": sms, "ms_per_step_nccl_allgather": gms if world > 1 else None,
+        "kernel_ms_per_rank": kms,
+        "parity_vs_local_128_heads": {"fused_bitwise_equal": bool(parity[0].item()),
+                                      "nccl_bitwise_equal": bool(parity[1].item()),
+                                      "fused_max_abs_diff": maxdiff[0].item(),
+                                      "nccl_max_abs_diff": maxdiff[1].item()},
+        "roofline": {"bound": "hbm", "kernel": "dsa_attention_kernel",
+                     "achieved": ab / (kms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": ab / (kms / 1e3) / 1e9 / peak,
+                     "note": "algorithmic bytes per rank = 16-head operator bytes x head groups"},
+        "gpu_launches_per_step": 3 if world > 1 else 2,  # attention + merge (+ peer barrier)
+    }
+
+
+def run_cfg3(args):
+    """BASELINE cfg3 alone (see measure_cfg3); strong scaling, the job is fixed."""
+    rank, world, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import torch.distributed as dist
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    r = measure_cfg3(dev, world, rank, args.steps, args.warmup, dist)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "DSA decode query-tokens/sec, 128 heads (head-sharded)", "value": r["value"],
+            "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": r["ms_per_step_fused_gather"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded, BASELINE cfg3 shapes and distributions)",
+            "config": {"workload": r["workload"], "parallelism": r["parallelism"], "l2": L2_NOTE},
+            "cfg3": r, "roofline": dict(r["roofline"], traffic=None),
+            "gpu_launches": args.steps * r["gpu_launches_per_step"],
+        }), flush=True)
+    if world > 1:
         dist.destroy_process_group()
 
 

@@ -35,6 +35,7 @@ SIGNATURES = {
                              I64, I64, I64, I64, I64, F32, P, I64, I64, P, I64, I64, P, SZ, P],
     "dsa_sparse_attention_noalloc": [P, I64, I64, P, I64, I64, P, I64, I64, P, I64, I64, P, I64,
                                      I64, I64, I64, I64, I64, F32, P, I64, I64, P, I64, I64, P],
+    "dsa_sparse_attention_noalloc_read_error": [INT, ctypes.POINTER(INT), P],
     "dsa_sparse_attention_scatter": [P, I64, I64, P, I64, I64, P, I64, I64, P, I64, I64, P, I64,
                                      I64, I64, I64, I64, I64, F32, P, I64, I64, P, I64, I64, INT,
                                      P, SZ, P],

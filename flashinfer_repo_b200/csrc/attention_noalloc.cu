@@ -11,18 +11,27 @@
 // library's own device memory.
 //
 // Facts a caller must know:
-//  * The array takes kNoAllocScratchBytes (about 20 MiB) on EVERY device that
-//    loads this library, for as long as the process runs.
-//  * Limits: num_tokens * num_heads / 16 <= kNoAllocMaxVirtualTokens, and the
-//    kernel's grid must fit kNoAllocMaxCtas CTAs; larger calls are rejected
-//    with DSA_ERR_UNSUPPORTED and a message, nothing is launched.
+//  * The array takes kNoAllocScratchBytes (about 20 MiB) on every device where
+//    it is used, for as long as the process runs.  With CUDA's default lazy
+//    module loading the array is placed in device memory when this file's code
+//    is first used on a device, i.e. by the first call: make that first call
+//    (a warm-up call) before the engine reserves its memory pool, or run with
+//    CUDA_MODULE_LOADING=EAGER so that it is placed when the library loads.
+//  * Limit: the scratch holds the split-K partials of at most kNoAllocMaxCtas
+//    CTAs (two slots each).  The default launch plan on a B200 uses at most
+//    2 x 148 = 296 CTAs for any batch, so every shape the operator accepts
+//    fits; only a plan forced larger through dsa_set_options is rejected with
+//    DSA_ERR_UNSUPPORTED and a message, and nothing is launched.
 //  * The first call on a device looks up the array's device address (once per
 //    device, with that device current); make that first call before any stream
 //    capture begins.
 //  * All calls on a device share the one array and it keeps the last call's
 //    contents.  Calls whose executions overlap on the GPU (different streams,
 //    or several host threads) race on it and give wrong results; serialise
-//    them.  Each call clears the error word.
+//    them.
+//  * Device errors (a bad index, a timed-out wait) accumulate in the array's
+//    error word across calls until dsa_sparse_attention_noalloc_read_error
+//    reads (and optionally clears) it; it starts at zero.
 //  * No cudaMalloc, cudaFree or other allocating routine is called.
 #include <mutex>
 
@@ -31,7 +40,6 @@
 
 namespace {
 
-constexpr size_t kNoAllocMaxVirtualTokens = 8192;
 constexpr size_t kNoAllocMaxCtas = 320;
 constexpr size_t kPartBytes = (16 * 512 + 2 * 16) * sizeof(float);  // one split-K partial
 constexpr size_t kCounterBytes = 256;  // error word
@@ -45,6 +53,24 @@ void* g_scratch_ptr[64] = {};  // device address of g_noalloc_scratch, per devic
 
 // Messages go through the library's error channel (dsa_last_error_message).
 int dsa_noalloc_fail(int code, const char* msg) { return dsa::report_error(code, msg); }
+
+// Device address of the scratch array on the current device, looked up once
+// per device (cudaGetSymbolAddress with that device current).
+int scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64)
+    return dsa_noalloc_fail(DSA_ERR_CUDA, "dsa_sparse_attention_noalloc: no current CUDA device");
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) return dsa_noalloc_fail(DSA_ERR_CUDA, cudaGetErrorString(e));
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return DSA_OK;
+}
 
 }  // namespace
 
@@ -64,43 +90,19 @@ extern "C" int dsa_sparse_attention_noalloc(
                                 num_pages, page_size, topk, sm_scale, output, out_stride_token,
                                 out_stride_head, lse, lse_stride_token, lse_stride_head, nullptr, 0,
                                 stream);  // reports the argument error
-  const int64_t vtokens = num_tokens * (num_heads / 16);
-  if ((size_t)vtokens > kNoAllocMaxVirtualTokens) {
-    return dsa_noalloc_fail(DSA_ERR_UNSUPPORTED,
-                            "dsa_sparse_attention_noalloc: num_tokens*num_heads/16 exceeds the "
-                            "8192 the static scratch holds; use dsa_sparse_attention");
-  }
   if (num_tokens == 0) return DSA_OK;
-
-  // Once per device: the device address of the scratch array.
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= 64)
-    return dsa_noalloc_fail(DSA_ERR_CUDA, "dsa_sparse_attention_noalloc: no current CUDA device");
   void* scratch = nullptr;
-  {
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_scratch_ptr[dev]) {
-      void* p = nullptr;
-      e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-      if (e != cudaSuccess || !p)
-        return dsa_noalloc_fail(DSA_ERR_CUDA, cudaGetErrorString(e));
-      g_scratch_ptr[dev] = p;
-    }
-    scratch = g_scratch_ptr[dev];
-  }
+  int rc = scratch_address(&scratch);
+  if (rc != DSA_OK) return rc;
 
   size_t need = 0;
-  int rc = dsa_sparse_attention_workspace_size(num_tokens, num_heads, topk, &need);
+  rc = dsa_sparse_attention_workspace_size(num_tokens, num_heads, topk, &need);
   if (rc != DSA_OK) return rc;
   if (need > kNoAllocScratchBytes)
     return dsa_noalloc_fail(DSA_ERR_UNSUPPORTED,
-                            "dsa_sparse_attention_noalloc: this shape needs more split-K scratch "
-                            "than the static array holds; use dsa_sparse_attention");
-
-  // The error word starts at zero.
-  e = cudaMemsetAsync(scratch, 0, sizeof(int), static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) return dsa_noalloc_fail(DSA_ERR_CUDA, cudaGetErrorString(e));
+                            "dsa_sparse_attention_noalloc: the launch plan has more than the 320 "
+                            "CTAs whose split-K partials the static array holds; use "
+                            "dsa_sparse_attention");
 
   return dsa_sparse_attention(q_nope, q_nope_stride_token, q_nope_stride_head, q_pe,
                               q_pe_stride_token, q_pe_stride_head, ckv_cache, ckv_stride_page,
@@ -109,4 +111,12 @@ extern "C" int dsa_sparse_attention_noalloc(
                               page_size, topk, sm_scale, output, out_stride_token, out_stride_head,
                               lse, lse_stride_token, lse_stride_head, scratch,
                               kNoAllocScratchBytes, stream);
+}
+
+extern "C" int dsa_sparse_attention_noalloc_read_error(int clear, int* bits, void* stream) {
+  if (!bits) return dsa_noalloc_fail(DSA_ERR_INVALID_ARG, "bits is NULL");
+  void* scratch = nullptr;
+  const int rc = scratch_address(&scratch);
+  if (rc != DSA_OK) return rc;
+  return dsa_read_device_error(scratch, clear, bits, stream);
 }

@@ -180,13 +180,19 @@ int dsa_peer_barrier(int* const* flags, int rank, int world, int* device_error, 
  * nearly all free HBM for the KV cache at start-up and pass every later
  * allocation through their own pool, and plugin hosts that hand an operator
  * only its inputs and outputs, with no workspace and no allocator.  The
- * scratch lives in a static device array of the library (about 20 MiB on
- * every device that loads it, held until the process exits).  Limits:
- * num_tokens*num_heads/16 <= 8192 and a grid of at most 320 CTAs; larger calls
- * return DSA_ERR_UNSUPPORTED without launching.  The first call on a device
- * looks up the array's address (do it before any stream capture).  All calls
- * on a device share the array: calls that overlap on the GPU race and must be
- * serialised by the caller.  No cudaMalloc/cudaFree is called.
+ * scratch lives in a static device array of the library (about 20 MiB per
+ * device, held until the process exits).  Under CUDA's default lazy module
+ * loading that array takes its device memory at the first call on a device,
+ * so make a first (warm-up) call before the engine reserves its memory, or
+ * set CUDA_MODULE_LOADING=EAGER.  Limit: the split-K partials of at most 320
+ * CTAs, which every default launch plan on a B200 (at most 296 CTAs) fits;
+ * a plan forced larger through dsa_set_options returns DSA_ERR_UNSUPPORTED
+ * without launching.  The first call on a device also looks up the array's
+ * address (do it before any stream capture).  All calls on a device share the
+ * array: calls that overlap on the GPU race and must be serialised by the
+ * caller.  Device errors accumulate in the array's error word until
+ * dsa_sparse_attention_noalloc_read_error reads it.  No cudaMalloc/cudaFree
+ * is called.
  */
 int dsa_sparse_attention_noalloc(const void* q_nope, int64_t q_nope_stride_token,
                                  int64_t q_nope_stride_head, const void* q_pe,
@@ -199,6 +205,13 @@ int dsa_sparse_attention_noalloc(const void* q_nope, int64_t q_nope_stride_token
                                  int64_t page_size, int64_t topk, float sm_scale, void* output,
                                  int64_t out_stride_token, int64_t out_stride_head, float* lse,
                                  int64_t lse_stride_token, int64_t lse_stride_head, void* stream);
+
+/*
+ * Read (and, with clear != 0, reset) the DSA_DEVERR_* bits that calls of
+ * dsa_sparse_attention_noalloc on the current device have raised since the
+ * last clear.  Synchronises the stream.  No counterpart in the reference.
+ */
+int dsa_sparse_attention_noalloc_read_error(int clear, int* bits, void* stream);
 
 /*
  * FP8 lightning-indexer scores.  Replaces indexer_kernel
