@@ -880,7 +880,8 @@ def run_cfg5(args):
         dist.init_process_group("nccl", device_id=dev)
     from flashinfer_repo_b200 import kernel
     from flashinfer_repo_b200.bench_inputs import attention_bytes, attention_flops, make_prefill_device
-    qn, qp, ckv, kpe, idx, scale = make_prefill_device(seed=5000 + rank, device=dev)
+    qn, qp, ckv, kpe, idx, scale = make_prefill_device(seed=5000 + rank, device=dev,
+                                                       queries=args.queries)
     T = idx.shape[0]
     out = torch.empty((T, 16, 512), dtype=torch.bfloat16, device=dev)
     lse = torch.empty((T, 16), dtype=torch.float32, device=dev)
@@ -915,7 +916,8 @@ def run_cfg5(args):
             "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": kms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded, BASELINE cfg5 shapes and distributions)",
-            "config": {"workload": "cfg5: 4096 queries/GPU, ctx 65536, causal top-2048, 16 heads",
+            "config": {"workload": f"cfg5: {T} queries/GPU, ctx 65536, causal top-2048, 16 heads",
+                       "attention_kernel": args.attention_kernel,
                        "l2": L2_NOTE + "; the 72 MiB cache is re-read from L2 within a step"},
             "roofline": {"bound": "hbm (per-token formula)", "achieved": ab / (kms / 1e3) / 1e9, "peak": peak,
                          "unit": "GB/s", "frac": ab / (kms / 1e3) / 1e9 / peak, "traffic": None},
@@ -937,7 +939,13 @@ def main():
     ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg3", "cfg4", "cfg5"],
                     help="cfg2 = headline batched decode; cfg4 = indexer + top-k + attention")
     ap.add_argument("--requests", type=int, default=128, help="cfg4 requests per GPU (default 128)")
+    ap.add_argument("--queries", type=int, default=4096, help="cfg5 query tokens per GPU (default 4096)")
+    ap.add_argument("--attention-kernel", type=int, default=0, choices=[0, 1, 2],
+                    help="library option attention_kernel: 0 default, 1 mma.sync, 2 tcgen05")
     args = ap.parse_args()
+    if args.attention_kernel and args.impl == "ours":
+        from flashinfer_repo_b200 import set_options
+        set_options(attention_kernel=args.attention_kernel)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -74,6 +74,21 @@ def build(force: bool = False, verbose: bool = False) -> str:
     return LIB
 
 
+PROBES = os.path.join(PKG, "probes")
+
+
+def build_probes(force: bool = False) -> list:
+    """Compile the measurement probes in probes/*.cu (standalone programs, not
+    part of the library) next to their sources."""
+    outs = []
+    for src in sorted(glob.glob(os.path.join(PROBES, "*.cu"))):
+        exe = src[:-3]
+        if force or _stale(exe, [src] + glob.glob(os.path.join(CSRC, "*.cuh"))):
+            subprocess.check_call([nvcc()] + NVCC_FLAGS + ["-o", exe, src, "-lcuda"])
+        outs.append(exe)
+    return outs
+
+
 def build_contest_binding(force: bool = False) -> str | None:
     """Compile the contest route's TVM-FFI binding (contest/binding.cu) for
     sm_100a into _build/ as a check that it builds; the contest harness itself
@@ -94,3 +109,5 @@ def build_contest_binding(force: bool = False) -> str | None:
 
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    if "--probes" in sys.argv:
+        print("\n".join(build_probes(force="--force" in sys.argv)))
