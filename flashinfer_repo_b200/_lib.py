@@ -39,6 +39,9 @@ SIGNATURES = {
     "dsa_sparse_attention_scatter": [P, I64, I64, P, I64, I64, P, I64, I64, P, I64, I64, P, I64,
                                      I64, I64, I64, I64, I64, F32, P, I64, I64, P, I64, I64, INT,
                                      P, SZ, P],
+    "dsa_sparse_attention_scatter_sync": [P, I64, I64, P, I64, I64, P, I64, I64, P, I64, I64, P, I64,
+                                          I64, I64, I64, I64, I64, F32, P, I64, I64, P, I64, I64,
+                                          INT, P, INT, INT, P, SZ, P],
     "dsa_peer_alloc": [SZ, ctypes.POINTER(P), P],
     "dsa_peer_open": [P, ctypes.POINTER(P)],
     "dsa_peer_close": [P],

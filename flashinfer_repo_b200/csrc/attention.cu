@@ -75,6 +75,15 @@ struct AttnParams {
   int n_peers;
   float* part;
   int* err;
+  // Cross-GPU barrier after the last store (head-parallel decode), when
+  // sync_world > 0: the last CTA to finish in the grid that stores last (the
+  // merge grid when one runs, else the attention grid) announces this rank's
+  // next epoch to every rank and waits, bounded, until all ranks announced it.
+  // sync_flags[q]: rank q's flag buffer as mapped in this process; int32
+  // layout [0] this rank's epoch, [1 + q] the epoch rank q announced here,
+  // [9] CTAs of the current launch that finished (back to 0 after it).
+  int* sync_flags[kMaxTargets];
+  int sync_rank, sync_world, sync_in_merge;
 };
 
 template <int NST>
@@ -102,6 +111,40 @@ __device__ __forceinline__ int cta_of_tile(const AttnParams& p, int tile) {
 __device__ __forceinline__ float* part_slot(const AttnParams& p, int c, int v) {
   const int j = (v == cta_start(p, c) / p.tiles_per_token) ? 0 : 1;
   return p.part + (int64_t)(2 * c + j) * kPartFloats;
+}
+
+__device__ __forceinline__ void st_release_sys(int* ptr, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* ptr) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
+// Called by one thread per CTA after a CTA-wide barrier that follows all of
+// the CTA's stores.  The last of the grid's `nctas` CTAs runs the cross-GPU
+// barrier: its release stores carry every store the grid (and, through grid
+// completion, the attention grid before it) made, peer stores included.
+__device__ void grid_done_then_sync(const AttnParams& p, unsigned nctas) {
+  __threadfence_system();
+  int* mine = p.sync_flags[p.sync_rank];
+  const unsigned prev = atomicAdd(reinterpret_cast<unsigned*>(mine + 9), 1u);
+  if (prev != nctas - 1) return;
+  __threadfence_system();
+  mine[9] = 0;
+  const int epoch = mine[0] + 1;
+  for (int q = 0; q < p.sync_world; ++q) st_release_sys(p.sync_flags[q] + 1 + p.sync_rank, epoch);
+  const long long t0 = clock64();
+  for (int q = 0; q < p.sync_world; ++q) {
+    while (ld_acquire_sys(mine + 1 + q) < epoch) {
+      if (clock64() - t0 > kWaitBudgetCycles) {
+        set_error(p.err, kErrTimeout);
+        break;
+      }
+    }
+  }
+  mine[0] = epoch;
 }
 
 __device__ __forceinline__ int n_targets(const AttnParams& p) { return p.n_peers > 0 ? p.n_peers : 1; }
@@ -196,12 +239,9 @@ __device__ __forceinline__ void attn_producer(const AttnParams& p, AttnSmem<NST>
 constexpr int kMergeThreads = 128;
 constexpr int kMergeChunk = 8;
 
-__global__ void __launch_bounds__(kMergeThreads) dsa_attention_merge_kernel(const __grid_constant__ AttnParams p) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");  // attention grid done, writes visible
-  const int h = blockIdx.x, v = blockIdx.y, i = threadIdx.x;
+__device__ __forceinline__ void merge_token(const AttnParams& p, int h, int v, int i, int c_first,
+                                            int c_last) {
   const int tpt = p.tiles_per_token;
-  const int c_first = cta_of_tile(p, v * tpt), c_last = cta_of_tile(p, v * tpt + tpt - 1);
-  if (c_first == c_last) return;  // written directly by the attention kernel
   // Slot of partial c: every CTA after c_first starts inside this token (its
   // first segment, slot 0); c_first holds it in slot 1 unless it starts at
   // the token's first tile.
@@ -255,6 +295,18 @@ __global__ void __launch_bounds__(kMergeThreads) dsa_attention_merge_kernel(cons
     if (i == 0)
       lse_target(p, k)[t * p.lse_st + (int64_t)(grp * kHeads + h) * p.lse_sh] =
           (M == -INFINITY) ? -INFINITY : M + log2f(L);
+  }
+}
+
+__global__ void __launch_bounds__(kMergeThreads) dsa_attention_merge_kernel(const __grid_constant__ AttnParams p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // attention grid done, writes visible
+  const int h = blockIdx.x, v = blockIdx.y, i = threadIdx.x;
+  const int tpt = p.tiles_per_token;
+  const int c_first = cta_of_tile(p, v * tpt), c_last = cta_of_tile(p, v * tpt + tpt - 1);
+  if (c_first != c_last) merge_token(p, h, v, i, c_first, c_last);  // else written by the attention grid
+  if (p.sync_world > 0 && p.sync_in_merge) {
+    __syncthreads();
+    if (i == 0) grid_done_then_sync(p, gridDim.x * gridDim.y);
   }
 }
 
@@ -496,6 +548,10 @@ __global__ void __launch_bounds__(kThreads, (NST == 2 ? 2 : 1)) dsa_attention_ke
         __stcg(ps + kHeads * kDc + kHeads + g + 8, l1);
       }
     }
+  }
+  if (p.sync_world > 0 && !p.sync_in_merge) {  // no merge grid: this grid stores last
+    named_bar_sync(1, kCWarps * 32);
+    if (threadIdx.x == 0) grid_done_then_sync(p, gridDim.x);
   }
   // This CTA's results are written: the merge grid (launched as a dependent)
   // may start its prologue; it still waits for this whole grid to finish.
@@ -1059,7 +1115,8 @@ static int attention_impl(const void* q_nope, int64_t q_nope_stride_token, int64
                          int64_t topk, float sm_scale, void* output, int64_t out_stride_token,
                          int64_t out_stride_head, float* lse, int64_t lse_stride_token,
                          int64_t lse_stride_head, void* workspace, size_t workspace_bytes,
-                         void* stream, void* const* out_peers, float* const* lse_peers, int n_peers) {
+                         void* stream, void* const* out_peers, float* const* lse_peers, int n_peers,
+                         int* const* sync_flags = nullptr, int sync_rank = 0, int sync_world = 0) {
   if (num_tokens < 0) return fail(DSA_ERR_INVALID_ARG, "num_tokens < 0");
   if (num_heads <= 0 || num_heads % kHeads)
     return fail(DSA_ERR_UNSUPPORTED, "num_heads must be a positive multiple of 16");
@@ -1096,7 +1153,15 @@ static int attention_impl(const void* q_nope, int64_t q_nope_stride_token, int64
   const bool q16 = !(reinterpret_cast<uintptr_t>(q_nope) & 15) && !(reinterpret_cast<uintptr_t>(q_pe) & 15) &&
                    q_nope_stride_token % 8 == 0 && q_nope_stride_head % 8 == 0 &&
                    q_pe_stride_token % 8 == 0 && q_pe_stride_head % 8 == 0;
-  const bool tc = tc_choice(opt) && topk % kTcRows == 0 && q16;
+  if (sync_world > 0) {
+    if (!sync_flags || sync_world > kMaxTargets || sync_rank < 0 || sync_rank >= sync_world)
+      return fail(DSA_ERR_INVALID_ARG, "world must be 1..8 and 0 <= rank < world");
+    for (int q = 0; q < sync_world; ++q)
+      if (!sync_flags[q] || (reinterpret_cast<uintptr_t>(sync_flags[q]) & 3))
+        return fail(DSA_ERR_INVALID_ARG, "NULL or misaligned flag buffer");
+  }
+  // the cross-GPU barrier runs inside the mma.sync kernel's grids only
+  const bool tc = tc_choice(opt) && topk % kTcRows == 0 && q16 && sync_world == 0;
   Plan pl;
   int rc = make_plan(num_tokens, num_heads, topk, nst, &pl, tc, opt);
   if (rc) return rc;
@@ -1138,11 +1203,15 @@ static int attention_impl(const void* q_nope, int64_t q_nope_stride_token, int64
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   p.err = reinterpret_cast<int*>(ws);
   p.part = reinterpret_cast<float*>(ws + pl.part_off);
+  p.sync_world = sync_world;
+  p.sync_rank = sync_rank;
+  p.sync_in_merge = pl.ctas > 1 ? 1 : 0;
+  for (int q = 0; q < kMaxTargets; ++q) p.sync_flags[q] = q < sync_world ? sync_flags[q] : nullptr;
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // Profiling option attention_grids: 1 = attention grid only, 2 = merge grid
   // only (on the partials of an earlier call with the same shapes); 0 both.
-  const int stage = opt.attention_grids;
+  const int stage = sync_world > 0 ? 0 : opt.attention_grids;  // the barrier needs both grids
   cudaError_t e = cudaSuccess;
   if (stage != 2) {
     if (tc) {
@@ -1260,6 +1329,29 @@ int dsa_sparse_attention_scatter(const void* q_nope, int64_t q_nope_stride_token
                         num_tokens, num_heads, num_pages, page_size, topk, sm_scale, nullptr,
                         out_stride_token, out_stride_head, nullptr, lse_stride_token, lse_stride_head,
                         workspace, workspace_bytes, stream, out_targets, lse_targets, num_targets);
+}
+
+int dsa_sparse_attention_scatter_sync(
+    const void* q_nope, int64_t q_nope_stride_token, int64_t q_nope_stride_head, const void* q_pe,
+    int64_t q_pe_stride_token, int64_t q_pe_stride_head, const void* ckv_cache, int64_t ckv_stride_page,
+    int64_t ckv_stride_row, const void* kpe_cache, int64_t kpe_stride_page, int64_t kpe_stride_row,
+    const int32_t* sparse_indices, int64_t indices_stride_token, int64_t num_tokens, int64_t num_heads,
+    int64_t num_pages, int64_t page_size, int64_t topk, float sm_scale, void* const* out_targets,
+    int64_t out_stride_token, int64_t out_stride_head, float* const* lse_targets,
+    int64_t lse_stride_token, int64_t lse_stride_head, int num_targets, int* const* flags, int rank,
+    int world, void* workspace, size_t workspace_bytes, void* stream) {
+  if (num_targets <= 0 || num_targets > kMaxTargets)
+    return fail(DSA_ERR_INVALID_ARG, "num_targets must be in 1..8");
+  if (world <= 0) return fail(DSA_ERR_INVALID_ARG, "world must be 1..8 and 0 <= rank < world");
+  if (num_tokens == 0)  // nothing to store: the ranks still meet
+    return dsa_peer_barrier(flags, rank, world, reinterpret_cast<int*>(workspace), stream);
+  return attention_impl(q_nope, q_nope_stride_token, q_nope_stride_head, q_pe, q_pe_stride_token,
+                        q_pe_stride_head, ckv_cache, ckv_stride_page, ckv_stride_row, kpe_cache,
+                        kpe_stride_page, kpe_stride_row, sparse_indices, indices_stride_token,
+                        num_tokens, num_heads, num_pages, page_size, topk, sm_scale, nullptr,
+                        out_stride_token, out_stride_head, nullptr, lse_stride_token, lse_stride_head,
+                        workspace, workspace_bytes, stream, out_targets, lse_targets, num_targets,
+                        flags, rank, world);
 }
 
 int dsa_read_device_error(const void* workspace, int clear, int* bits, void* stream) {

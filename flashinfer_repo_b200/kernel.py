@@ -184,12 +184,15 @@ def _launch(fn, q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, nu
 
 
 def kernel_scatter(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, out_ptrs,
-                   lse_ptrs, out_strides, lse_strides):
+                   lse_ptrs, out_strides, lse_strides, sync=None):
     """`kernel` whose results are stored into every (out_ptrs[k], lse_ptrs[k])
     target (device addresses, peer GPUs' included, each offset to where these
     heads belong; up to 8) with the given (token, head) element strides,
-    instead of into freshly allocated tensors.  Returns nothing; the caller
-    orders the stores (e.g. with a peer barrier)."""
+    instead of into freshly allocated tensors.  Returns nothing.  Without
+    `sync` the caller orders the stores (e.g. with a peer barrier); with
+    sync = (flags, rank, world) -- flags a ctypes array of the ranks' flag
+    buffers as mapped here -- the operator ends with that cross-GPU barrier
+    itself (dsa_sparse_attention_scatter_sync)."""
     num_tokens, heads, num_pages, topk = _check_inputs(q_nope, q_pe, ckv_cache, kpe_cache,
                                                        sparse_indices)
     n = len(out_ptrs)
@@ -198,10 +201,16 @@ def kernel_scatter(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale,
         return
     outs = (ctypes.c_void_p * n)(*out_ptrs)
     lses = (ctypes.c_void_p * n)(*lse_ptrs)
-    _launch("dsa_sparse_attention_scatter", q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices,
-            sm_scale, num_tokens, heads, num_pages, topk,
-            (ctypes.cast(outs, ctypes.c_void_p), int(out_strides[0]), int(out_strides[1]),
-             ctypes.cast(lses, ctypes.c_void_p), int(lse_strides[0]), int(lse_strides[1]), n))
+    targets = (ctypes.cast(outs, ctypes.c_void_p), int(out_strides[0]), int(out_strides[1]),
+               ctypes.cast(lses, ctypes.c_void_p), int(lse_strides[0]), int(lse_strides[1]), n)
+    if sync is None:
+        _launch("dsa_sparse_attention_scatter", q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices,
+                sm_scale, num_tokens, heads, num_pages, topk, targets)
+    else:
+        flags, rank, world = sync
+        _launch("dsa_sparse_attention_scatter_sync", q_nope, q_pe, ckv_cache, kpe_cache,
+                sparse_indices, sm_scale, num_tokens, heads, num_pages, topk,
+                targets + (ctypes.cast(flags, ctypes.c_void_p), int(rank), int(world)))
 
 
 def kernel_splitk(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, SPLIT_K=None):

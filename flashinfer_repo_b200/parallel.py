@@ -98,8 +98,10 @@ class PeerHeadShardedAttention:
     with two [T, H, 512] bf16 outputs, two [T, H] fp32 LSE arrays and the
     barrier flags.  A call computes this rank's H/world heads with
     `dsa_sparse_attention_scatter`, whose epilogues store each result row
-    into the same place of EVERY rank's buffer (plain stores over NVLink), then
-    runs `dsa_peer_barrier`; after it the local buffer holds all H heads.
+    into the same place of EVERY rank's buffer (plain stores over NVLink), and
+    its last grid ends with the cross-GPU barrier
+    (`dsa_sparse_attention_scatter_sync`); after it the local buffer holds all
+    H heads.
     Calls alternate between the two buffers.  Rule for the caller: read the
     returned tensors on the current stream before issuing the next call.
     Then the barrier of call n+1 follows every rank's reads of call n's
@@ -159,7 +161,7 @@ class PeerHeadShardedAttention:
         dist.barrier(group=group)  # every rank mapped every buffer before the first store
 
     def __call__(self, q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale):
-        from .kernel import kernel_scatter, workspace_for
+        from .kernel import kernel_scatter
         T, H, _ = q_nope.shape
         assert (T, H) == (self.T, self.H), "shapes are fixed at construction"
         b = self.step & 1
@@ -167,16 +169,23 @@ class PeerHeadShardedAttention:
         head0 = self.h * self.rank
         outs = [p + self.off_out[b] + head0 * DC * 2 for p in self.ptrs]
         lses = [p + self.off_lse[b] + head0 * 4 for p in self.ptrs]
+        # one operator call: epilogues store into every rank's buffer, and the
+        # grid that stores last ends with the cross-GPU barrier
         kernel_scatter(q_nope[:, sl], q_pe[:, sl], ckv_cache, kpe_cache, sparse_indices, sm_scale,
-                       outs, lses, (H * DC, DC), (H, 1))
+                       outs, lses, (H * DC, DC), (H, 1), sync=(self._flags, self.rank, self.world))
+        self.step += 1
+        return self.out[b], self.lse[b]
+
+    def barrier(self):
+        """A bare cross-GPU barrier on the current stream (dsa_peer_barrier),
+        e.g. to line the ranks up on the device before timing a step."""
+        from .kernel import workspace_for
         ws = workspace_for(self.device).buf
         with torch.cuda.device(self.device):
             stream = torch.cuda.current_stream(self.device).cuda_stream
             self._lib.call("dsa_peer_barrier", ctypes.cast(self._flags, ctypes.c_void_p), self.rank,
                            self.world, ws.data_ptr() if ws is not None else None,
                            ctypes.c_void_p(stream))
-        self.step += 1
-        return self.out[b], self.lse[b]
 
     def close(self):
         """Unmap the peers' buffers and free this rank's (after a host sync;

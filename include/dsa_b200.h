@@ -150,6 +150,30 @@ int dsa_sparse_attention_scatter(const void* q_nope, int64_t q_nope_stride_token
                                  void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * dsa_sparse_attention_scatter_sync -- dsa_sparse_attention_scatter followed by
+ * the cross-GPU barrier of dsa_peer_barrier, run inside the operator: the last
+ * CTA to finish in the grid that stores last announces this rank's next epoch
+ * to every rank (release stores at system scope, after all of the call's
+ * stores, peer stores included) and waits, bounded, until every rank has
+ * announced it.  When it completes on the stream, every rank's stores of this
+ * step are visible in every target buffer.  flags[q] is rank q's flag buffer
+ * (>= 10 int32, zeroed, from dsa_peer_alloc) as mapped in this process; the
+ * same buffers serve dsa_peer_barrier, and the two can be mixed as long as
+ * every rank issues the same sequence.  A timed-out wait sets
+ * DSA_DEVERR_TIMEOUT in the workspace's error word.  No counterpart in the
+ * single-GPU reference.
+ */
+int dsa_sparse_attention_scatter_sync(
+    const void* q_nope, int64_t q_nope_stride_token, int64_t q_nope_stride_head, const void* q_pe,
+    int64_t q_pe_stride_token, int64_t q_pe_stride_head, const void* ckv_cache, int64_t ckv_stride_page,
+    int64_t ckv_stride_row, const void* kpe_cache, int64_t kpe_stride_page, int64_t kpe_stride_row,
+    const int32_t* sparse_indices, int64_t indices_stride_token, int64_t num_tokens, int64_t num_heads,
+    int64_t num_pages, int64_t page_size, int64_t topk, float sm_scale, void* const* out_targets,
+    int64_t out_stride_token, int64_t out_stride_head, float* const* lse_targets,
+    int64_t lse_stride_token, int64_t lse_stride_head, int num_targets, int* const* flags, int rank,
+    int world, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Peer buffers and the cross-GPU barrier used with dsa_sparse_attention_scatter
  * (one process per GPU on one node; no counterpart in the single-GPU reference).
  *   dsa_peer_alloc  -- cudaMalloc `bytes` (zeroed) and export a CUDA IPC handle
