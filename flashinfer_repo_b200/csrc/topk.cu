@@ -38,13 +38,16 @@ __device__ __forceinline__ uint32_t ordered_key(float x) {
 // 2. Adaptive radix select: bins span the current range (bin = (key - lo) >>
 //    shift, at most kBins), so even the first pass spreads a real score
 //    distribution; each pass keeps the bin holding the k-th largest key until
-//    the range is one key T (at most three passes; later passes only count
-//    keys inside the range).  Eight histogram copies (one per four warps) cut
+//    the range is one key T.  Eight histogram copies (one per four warps) cut
 //    atomic contention; the bin is found with one block-wide scan (each thread
-//    sums two bins over the copies).
+//    sums two bins over the copies).  Full passes run only until the kept bin
+//    holds at most kMaxCand keys: a candidate pass then counts, per warp, the
+//    keys above the kept bin and copies the keys inside it into shared
+//    memory, and the remaining passes and the per-warp counts of step 3 run
+//    over those candidates.
 // 3. Selection in position order without atomics: warp w owns a contiguous
-//    chunk, lane l four consecutive keys per round.  A counting pass (plain
-//    per-thread sums) gives per-warp counts of keys > T and == T; one scan over
+//    chunk, lane l four consecutive keys per round.  Per-warp counts of keys
+//    > T and == T (from the candidate path, else a counting pass); one scan over
 //    the 32 warps gives each warp its output offset and its share of the
 //    wanted equal keys (ties go to the lowest positions); a writing pass
 //    places (key << 32 | ~position) words with one warp scan per round.
@@ -59,7 +62,8 @@ struct TopkSmem {
   uint32_t hist[kHistCopies][kBins];
   uint32_t red_lo[32], red_hi[32];
   uint32_t w_cnt[32], w_off[32], w_eqb[32];
-  uint32_t lo, hi, bstar, above;
+  uint32_t w_gt[32], w_ceq[32], w_cgt[32];  // candidate path: per-warp counts
+  uint32_t lo, hi, bstar, above, bcount, ncand;
   uint4 keys[kKeyCache / 4];
 };
 
@@ -224,14 +228,65 @@ __global__ void __launch_bounds__(kTopkThreads)
   uint32_t lo = S.lo, hi = S.hi;
   int need = n_out;
   const bool all = len <= k;
+  // warp w owns groups [w*cg, (w+1)*cg) in the selection passes, lane l takes
+  // group w*cg + r*32 + l in round r
+  const int cg = (((n4 + 31) / 32) + 31) / 32 * 32;
+  const int g0 = warp * cg, g1 = min(n4, g0 + cg);
+  // Block-wide search of a histogram in top-down order: the bin b* holding
+  // the need-th largest key and the count above it (thread t holds bins
+  // kBins-1-2t and kBins-2-2t, summed over `copies` copies `cstride` apart).
+  auto find_bin = [&](const uint32_t* h, int copies, int cstride, int nb, int want) {
+    const int d_hi = kBins - 1 - 2 * tid, d_lo = d_hi - 1;
+    uint32_t a = 0, c = 0;
+    for (int q = 0; q < copies; ++q) {
+      a += h[q * cstride + d_hi];
+      c += h[q * cstride + d_lo];
+    }
+    if (d_hi >= nb) a = 0;
+    if (d_lo >= nb) c = 0;
+    const uint32_t sum = a + c;
+    uint32_t incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) S.w_cnt[warp] = incl;
+    __syncthreads();
+    uint32_t wsum = lane < warp ? S.w_cnt[lane] : 0u;
+    wsum = __reduce_add_sync(0xffffffffu, wsum);
+    const uint32_t run = wsum + incl - sum;  // keys in bins above d_hi
+    if (run < (uint32_t)want && run + a >= (uint32_t)want) {
+      S.bstar = (uint32_t)d_hi;
+      S.above = run;
+      S.bcount = a;
+    } else if (run + a < (uint32_t)want && run + sum >= (uint32_t)want) {
+      S.bstar = (uint32_t)d_lo;
+      S.above = run + a;
+      S.bcount = c;
+    }
+    __syncthreads();
+  };
+  auto bin_shift = [](uint32_t range) {
+    int shift = 0;
+    while ((range >> shift) >= (uint32_t)kBins) ++shift;
+    return shift;
+  };
+  // Candidate path: after the first radix pass, one pass over the keys counts,
+  // per warp, the keys above the kept bin (all taken) and collects the keys
+  // inside it (at most kMaxCand) into shared memory; the rest of the radix
+  // select and the per-warp counts of the selection then run over the
+  // candidates only, so the later full passes (radix passes 2-3 and the
+  // counting pass of step 3) are skipped.  Too many candidates (heavy ties):
+  // the full passes run as before.
+  constexpr uint32_t kMaxCand = kHistCopies * kBins / 2;
+  bool counted = false;
   if (!all) {
     uint32_t* hist0 = &S.hist[0][0];
     uint32_t* mine = S.hist[warp & (kHistCopies - 1)];
     while (lo != hi) {
-      const uint32_t range = hi - lo;
-      int shift = 0;
-      while ((range >> shift) >= (uint32_t)kBins) ++shift;
-      const int nb = (int)(range >> shift) + 1;
+      const int shift = bin_shift(hi - lo);
+      const int nb = (int)((hi - lo) >> shift) + 1;
       for (int j = tid; j < kHistCopies * kBins; j += kTopkThreads) hist0[j] = 0;
       __syncthreads();
       for (int g = tid; g < n4; g += kTopkThreads) {
@@ -243,54 +298,95 @@ __global__ void __launch_bounds__(kTopkThreads)
         if (i + 3 < len && kk.w >= lo && kk.w <= hi) atomicAdd(&mine[(kk.w - lo) >> shift], 1u);
       }
       __syncthreads();
-      {
-        // bin b* (from the top) with count(above) < need <= count(above) + count(b*):
-        // thread t holds bins kBins-1-2t and kBins-2-2t (zero past nb), then a
-        // block-wide exclusive scan in top-down order
-        const int d_hi = kBins - 1 - 2 * tid, d_lo = d_hi - 1;
-        uint32_t a = 0, c = 0;
-#pragma unroll
-        for (int q = 0; q < kHistCopies; ++q) {
-          a += S.hist[q][d_hi];
-          c += S.hist[q][d_lo];
-        }
-        if (d_hi >= nb) a = 0;
-        if (d_lo >= nb) c = 0;
-        const uint32_t sum = a + c;
-        uint32_t incl = sum;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-          if (lane >= o) incl += y;
-        }
-        if (lane == 31) S.w_cnt[warp] = incl;
-        __syncthreads();
-        uint32_t wsum = lane < warp ? S.w_cnt[lane] : 0u;
-        wsum = __reduce_add_sync(0xffffffffu, wsum);
-        const uint32_t run = wsum + incl - sum;  // keys in bins above d_hi
-        if (run < (uint32_t)need && run + a >= (uint32_t)need) {
-          S.bstar = (uint32_t)d_hi;
-          S.above = run;
-        } else if (run + a < (uint32_t)need && run + sum >= (uint32_t)need) {
-          S.bstar = (uint32_t)d_lo;
-          S.above = run + a;
-        }
-      }
-      __syncthreads();
+      find_bin(hist0, kHistCopies, kBins, nb, need);
       const uint32_t d = S.bstar;
+      const uint32_t kept = S.bcount;
       need -= (int)S.above;
       const uint32_t nlo = lo + (d << shift);
       hi = (uint32_t)min((unsigned long long)hi, (unsigned long long)nlo + (1ull << shift) - 1ull);
       lo = nlo;
-      __syncthreads();  // S.bstar / S.above / the histograms are rewritten by the next pass
+      __syncthreads();  // S.bstar / S.above / the histograms are rewritten next
+      if (kept > kMaxCand) continue;  // another full pass narrows the bin first
+      // ---- candidate pass over this warp's groups: keys > hi are taken,
+      // keys in [lo, hi] are candidates (the histogram memory holds them)
+      unsigned long long* cand = reinterpret_cast<unsigned long long*>(hist0);
+      if (tid == 0) S.ncand = 0;
+      __syncthreads();
+      uint32_t n_gt = 0;
+      for (int gr = g0; gr < g1; gr += 32) {
+        const int g = gr + lane;
+        const uint4 kk = g < g1 ? group_at(g) : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t v[4] = {kk.x, kk.y, kk.z, kk.w};
+        uint32_t cm = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const bool in = g < g1 && 4 * g + q < len;
+          n_gt += (in && v[q] > hi) ? 1u : 0u;
+          cm |= (uint32_t)(in && v[q] >= lo && v[q] <= hi) << q;
+        }
+        if (__any_sync(0xffffffffu, cm != 0)) {  // most rounds hold no candidate
+          const uint32_t nc_l = __popc(cm);
+          uint32_t incl = nc_l;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+          }
+          uint32_t base = 0;
+          if (lane == 31) base = atomicAdd(&S.ncand, incl);
+          base = __shfl_sync(0xffffffffu, base, 31) + incl - nc_l;
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if ((cm >> q) & 1u) {
+              if (base < kMaxCand) cand[base] = ((unsigned long long)v[q] << 32) | (uint32_t)(4 * g + q);
+              ++base;
+            }
+        }
+      }
+      n_gt = __reduce_add_sync(0xffffffffu, n_gt);
+      if (lane == 0) {
+        S.w_gt[warp] = n_gt;
+        S.w_cgt[warp] = 0;
+        S.w_ceq[warp] = 0;
+      }
+      __syncthreads();
+      const uint32_t nc = S.ncand;  // == kept <= kMaxCand
+      // ---- radix select over the candidates (bins in buf, one copy)
+      uint32_t* h1 = reinterpret_cast<uint32_t*>(S.buf);
+      while (lo != hi) {
+        const int sh = bin_shift(hi - lo);
+        const int nb1 = (int)((hi - lo) >> sh) + 1;
+        for (int j = tid; j < kBins; j += kTopkThreads) h1[j] = 0;
+        __syncthreads();
+        for (uint32_t c = tid; c < nc; c += kTopkThreads) {
+          const uint32_t key = (uint32_t)(cand[c] >> 32);
+          if (key >= lo && key <= hi) atomicAdd(&h1[(key - lo) >> sh], 1u);
+        }
+        __syncthreads();
+        find_bin(h1, 1, 0, nb1, need);
+        const uint32_t d1 = S.bstar;
+        need -= (int)S.above;
+        const uint32_t nlo = lo + (d1 << sh);
+        hi = (uint32_t)min((unsigned long long)hi, (unsigned long long)nlo + (1ull << sh) - 1ull);
+        lo = nlo;
+        __syncthreads();
+      }
+      // ---- per-warp counts of candidates above / equal to the threshold
+      for (uint32_t c = tid; c < nc; c += kTopkThreads) {
+        const uint32_t key = (uint32_t)(cand[c] >> 32);
+        const int owner = (int)((cand[c] & 0xFFFFFFFFull) >> 2) / cg;
+        if (key > lo) atomicAdd(&S.w_cgt[owner], 1u);
+        else if (key == lo) atomicAdd(&S.w_ceq[owner], 1u);
+      }
+      __syncthreads();
+      if (tid < 32) S.w_cnt[tid] = ((S.w_gt[tid] + S.w_cgt[tid]) << 16) | S.w_ceq[tid];
+      counted = true;
+      __syncthreads();
     }
   }
   const uint32_t T = lo;  // with `all`, every key is taken
 
   // ---- 3. selection in position order
-  // warp w owns groups [w*cg, (w+1)*cg), lane l takes group w*cg + r*32 + l in round r
-  const int cg = (((n4 + 31) / 32) + 31) / 32 * 32;
-  const int g0 = warp * cg, g1 = min(n4, g0 + cg);
   auto flags = [&](const uint4& kk, int i, uint32_t& gt, uint32_t& eq) {
     const uint32_t v[4] = {kk.x, kk.y, kk.z, kk.w};
     gt = 0;
@@ -302,16 +398,18 @@ __global__ void __launch_bounds__(kTopkThreads)
       eq |= (uint32_t)(in && !all && v[q] == T) << q;
     }
   };
-  uint32_t n_gt = 0, n_eq = 0;
-  for (int g = g0 + lane; g < g1; g += 32) {
-    uint32_t gt, eq;
-    flags(group_at(g), 4 * g, gt, eq);
-    n_gt += __popc(gt);
-    n_eq += __popc(eq);
+  if (!counted) {  // counting pass (the candidate path has the counts already)
+    uint32_t n_gt = 0, n_eq = 0;
+    for (int g = g0 + lane; g < g1; g += 32) {
+      uint32_t gt, eq;
+      flags(group_at(g), 4 * g, gt, eq);
+      n_gt += __popc(gt);
+      n_eq += __popc(eq);
+    }
+    const uint32_t packed = __reduce_add_sync(0xffffffffu, (n_gt << 16) | n_eq);
+    if (lane == 0) S.w_cnt[warp] = packed;
+    __syncthreads();
   }
-  const uint32_t packed = __reduce_add_sync(0xffffffffu, (n_gt << 16) | n_eq);
-  if (lane == 0) S.w_cnt[warp] = packed;
-  __syncthreads();
   if (warp == 0) {
     const uint32_t pk = S.w_cnt[lane];
     const uint32_t g = pk >> 16, e = pk & 0xffffu;
