@@ -84,6 +84,7 @@ struct AttnParams {
   // [9] CTAs of the current launch that finished (back to 0 after it).
   int* sync_flags[kMaxTargets];
   int sync_rank, sync_world, sync_in_merge;
+  int merge_by_boundary;  // merge grid rows are CTA boundaries instead of tokens
 };
 
 template <int NST>
@@ -300,10 +301,21 @@ __device__ __forceinline__ void merge_token(const AttnParams& p, int h, int v, i
 
 __global__ void __launch_bounds__(kMergeThreads) dsa_attention_merge_kernel(const __grid_constant__ AttnParams p) {
   asm volatile("griddepcontrol.wait;" ::: "memory");  // attention grid done, writes visible
-  const int h = blockIdx.x, v = blockIdx.y, i = threadIdx.x;
+  const int h = blockIdx.x, i = threadIdx.x;
   const int tpt = p.tiles_per_token;
+  // Row y of the grid is virtual token y, or -- when there are more tokens than
+  // CTAs (prefill-sized batches, where only tokens that straddle a CTA
+  // boundary are split) -- the token holding CTA boundary y+1, merged by the
+  // first boundary inside it.
+  int v = blockIdx.y;
+  bool mine = true;
+  if (p.merge_by_boundary) {
+    const int c = blockIdx.y + 1, tile = cta_start(p, c);
+    v = tile / tpt;
+    mine = (tile % tpt != 0) && cta_of_tile(p, v * tpt) == c - 1;
+  }
   const int c_first = cta_of_tile(p, v * tpt), c_last = cta_of_tile(p, v * tpt + tpt - 1);
-  if (c_first != c_last) merge_token(p, h, v, i, c_first, c_last);  // else written by the attention grid
+  if (mine && c_first != c_last) merge_token(p, h, v, i, c_first, c_last);  // else written by the attention grid
   if (p.sync_world > 0 && p.sync_in_merge) {
     __syncthreads();
     if (i == 0) grid_done_then_sync(p, gridDim.x * gridDim.y);
@@ -1206,6 +1218,7 @@ static int attention_impl(const void* q_nope, int64_t q_nope_stride_token, int64
   p.sync_world = sync_world;
   p.sync_rank = sync_rank;
   p.sync_in_merge = pl.ctas > 1 ? 1 : 0;
+  p.merge_by_boundary = 0;
   for (int q = 0; q < kMaxTargets; ++q) p.sync_flags[q] = q < sync_world ? sync_flags[q] : nullptr;
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -1229,7 +1242,8 @@ static int attention_impl(const void* q_nope, int64_t q_nope_stride_token, int64
   if (e != cudaSuccess) return fail(DSA_ERR_CUDA, cudaGetErrorString(e));
   if (pl.ctas > 1 && stage != 1) {  // tokens split across CTAs: merge grid as a programmatic dependent
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(kHeads, (unsigned)pl.vtokens);
+    p.merge_by_boundary = pl.vtokens > pl.ctas - 1 ? 1 : 0;
+    cfg.gridDim = dim3(kHeads, (unsigned)(p.merge_by_boundary ? pl.ctas - 1 : pl.vtokens));
     cfg.blockDim = dim3(kMergeThreads);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = st;

@@ -61,6 +61,17 @@ def test_split_counts_agree(cuda_device, ctas):
         _oracle_check(case, cuda_device)
 
 
+@pytest.mark.parametrize("ctas", [16, 37])
+def test_more_tokens_than_ctas(cuda_device, ctas):
+    """More tokens than CTAs (the prefill-sized plan): only tokens straddling a
+    CTA boundary are split, and the merge grid runs one row per boundary."""
+    rng = np.random.default_rng(17)
+    case = W.make_attention_case(17, rng.integers(1500, 5000, size=40))
+    case.idx[3, :700] = -1
+    with options(attention_ctas=ctas, attention_min_tiles=1):
+        _oracle_check(case, cuda_device)
+
+
 @pytest.mark.parametrize("stages", [2, 3, 4])
 def test_pipeline_depths(cuda_device, stages):
     case = W.make_attention_case(8, [5000, 2100, 4096])
