@@ -1,6 +1,6 @@
 """Place the unmodified reference checkout in baseline/_ref (git-ignored).
 
-    python baseline/install_reference.py [/path/to/reference]
+    python baseline/install_reference.py /path/to/reference
 
 The reference (Starkdoorstep12/flashinfer-repo) has no setup.py or
 pyproject.toml, so `pip install --target baseline/_ref <reference>` cannot
@@ -41,4 +41,6 @@ def available() -> bool:
 
 
 if __name__ == "__main__":
-    print(install(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python baseline/install_reference.py /path/to/reference")
+    print(install(sys.argv[1]))

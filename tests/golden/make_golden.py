@@ -7,7 +7,7 @@ of the inputs.  The reference module only does `import torch, triton` and uses
 `math` without importing it (indexer_kernel.py:490), so `math` is injected
 into its namespace; the reference file itself is not modified.
 
-Usage:  python tests/golden/make_golden.py [/path/to/reference]
+Usage:  python tests/golden/make_golden.py /path/to/reference
 The GPU box never runs this script; it only reads the committed .npz files.
 """
 from __future__ import annotations
@@ -39,7 +39,7 @@ def bf16(bits: np.ndarray) -> torch.Tensor:
     return torch.from_numpy(bits.astype(np.int16)).view(torch.bfloat16)
 
 
-def main(ref_root: str = "/root/reference"):
+def main(ref_root: str):
     run = load_reference_run(ref_root)
     for name, make in CASES.items():
         c = make()
