@@ -49,9 +49,11 @@ sys.path.insert(0, ROOT)
 
 METRIC = "DSA decode query-tokens/sec (whole job); achieved HBM GB/s vs B200 peak"
 UNIT = "query_tokens/s"
-# dram__bytes_read.sum + dram__bytes_write.sum of one dsa_attention_kernel launch on
-# this workload: medians over 24 launches of an ncu launch list of this command
-ATTN_TRAFFIC_PER_LAUNCH = 153_366_784 + 1_001_984
+# dram__bytes_read.sum + dram__bytes_write.sum of one dsa_attention_kernel launch
+# captured on the small case of this workload (`--tokens 8`: 19,134,464 B read +
+# 512 B written for 19,218,944 algorithmic bytes); traffic grows with the rows
+# gathered, so a full launch is scaled by its algorithmic bytes
+ATTN_TRAFFIC_PER_ALG_BYTE = (19_134_464 + 512) / 19_218_944
 WORKLOAD = ("cfg2 batched decode: T=64 tokens/GPU, 16 heads, ckv512+kpe64 bf16, page 64, "
             "ctx U[1024,65536], topk 2048 (-1 padded), shuffled page tables")
 
@@ -364,7 +366,7 @@ def run_ours(args):
     from flashinfer_repo_b200 import kernel, read_device_error
     from flashinfer_repo_b200.bench_inputs import attention_bytes, make_cfg2_device
 
-    qn, qp, ckv, kpe, idx, scale = make_cfg2_device(seed=1000 + rank, device=dev)
+    qn, qp, ckv, kpe, idx, scale = make_cfg2_device(seed=1000 + rank, device=dev, T=args.tokens)
     T = idx.shape[0]
     alg_bytes = attention_bytes(idx)
     flush = L2Flush(dev)
@@ -417,7 +419,7 @@ def run_ours(args):
     # alternate between two independent batches (two 2.1 GB caches), so the
     # rows gathered by consecutive steps (2 x 151 MB) do not fit in L2.
     NB = 4
-    qn2, qp2, ckv2, kpe2, idx2, _ = make_cfg2_device(seed=5000 + rank, device=dev)
+    qn2, qp2, ckv2, kpe2, idx2, _ = make_cfg2_device(seed=5000 + rank, device=dev, T=args.tokens)
     batches = [(qn, qp, ckv, kpe, idx), (qn2, qp2, ckv2, kpe2, idx2)]
     # a step's inputs sit in one pinned staging buffer (q_nope | q_pe | indices,
     # 256-byte aligned parts), uploaded with one copy into a device buffer whose
@@ -577,11 +579,12 @@ def run_ours(args):
     peak, peak_kind = peaks()
 
     copies = copy_bandwidth(dev)
-    cfg4 = measure_cfg4(dev, rank, min(args.steps, 20), args.warmup, 128)
-    cfg3 = measure_cfg3(dev, world, rank, min(args.steps, 20), args.warmup, dist) if world > 1 else None
+    cfg4 = None if args.skip_extras else measure_cfg4(dev, rank, min(args.steps, 20), args.warmup, 128)
+    cfg3 = (measure_cfg3(dev, world, rank, min(args.steps, 20), args.warmup, dist)
+            if world > 1 and not args.skip_extras else None)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.skip_extras:
         os.sched_setaffinity(0, all_cpus)  # the CPU baseline uses every host core
         ref = reference_cpu_run(qn, qp, ckv, kpe, idx, scale, max_calls=3, budget_s=30.0)
         v, cores, sample = cpu_baseline_run(qn, qp, ckv, kpe, idx, scale)
@@ -604,8 +607,8 @@ def run_ours(args):
                        "launch": "value: steps as nodes of a CUDA graph (50 per graph), each step timed by its own event pair on the device; e2e: the public API with host copies",
                        "alg_bytes_per_step_per_gpu": alg_bytes},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": ATTN_TRAFFIC_PER_LAUNCH,
-                         "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
+                         "frac": achieved / peak, "traffic": round(ATTN_TRAFFIC_PER_ALG_BYTE * alg_bytes),
+                         "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum of the T=8 capture, scaled by algorithmic bytes)",
                          "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
                          "kernel": "dsa_attention_kernel", "avg_kernel_ms": avg_kernel_ms,
                          "step_ms_incl_merge_grid": statistics.mean(step_ms),
@@ -786,7 +789,7 @@ def measure_cfg3(dev, world, rank, steps, warmup, dist):
             flush(i)
             dist.barrier()
             torch.cuda.synchronize()
-            torch.cuda._sleep(200_000)
+            torch.cuda._sleep(2_000_000)  # ~1 ms of GPU work covers the host enqueue
             peer.barrier()  # ranks leave together on the device: host skew is not timed
             g0 = torch.cuda.Event(enable_timing=True)
             g1 = torch.cuda.Event(enable_timing=True)
@@ -804,7 +807,7 @@ def measure_cfg3(dev, world, rank, steps, warmup, dist):
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
-        torch.cuda._sleep(200_000)  # keeps the GPU busy while the host enqueues the step
+        torch.cuda._sleep(2_000_000)  # ~1 ms: the GPU stays busy while the host enqueues the step
         if world > 1:
             peer.barrier()  # ranks leave together on the device: host skew is not timed
         e[2].record(stream)
@@ -945,6 +948,10 @@ def main():
     ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg3", "cfg4", "cfg5"],
                     help="cfg2 = headline batched decode; cfg4 = indexer + top-k + attention")
     ap.add_argument("--requests", type=int, default=128, help="cfg4 requests per GPU (default 128)")
+    ap.add_argument("--tokens", type=int, default=64,
+                    help="cfg2 query tokens per GPU (default 64, the headline; smaller only for profiling)")
+    ap.add_argument("--skip-extras", action="store_true",
+                    help="omit the cfg4/cfg3 sub-objects and the CPU baseline (profiling runs)")
     ap.add_argument("--queries", type=int, default=4096, help="cfg5 query tokens per GPU (default 4096)")
     ap.add_argument("--attention-kernel", type=int, default=0, choices=[0, 1, 2],
                     help="library option attention_kernel: 0 default, 1 mma.sync, 2 tcgen05")
