@@ -23,7 +23,7 @@ class Options(ctypes.Structure):
     _fields_ = [("attention_kernel", ctypes.c_int), ("attention_stages", ctypes.c_int),
                 ("attention_ctas", ctypes.c_int), ("attention_min_tiles", ctypes.c_int),
                 ("attention_grids", ctypes.c_int), ("merge_pdl", ctypes.c_int),
-                ("indexer_tiles_per_cta", ctypes.c_int)]
+                ("indexer_tiles_per_cta", ctypes.c_int), ("attention_cluster", ctypes.c_int)]
 
 
 # name -> argtypes; every function returns int (dsa_status) except the message.

@@ -145,6 +145,34 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 // Host side: record `msg` as this thread's dsa_last_error_message() and return code.
 int report_error(int code, const char* msg);
 
+// Thread-block clusters: this CTA's rank, a cluster-wide barrier (every
+// thread of every CTA of the cluster arrives; release/acquire orders shared-
+// memory writes before it with reads of them after it), the shared::cluster
+// address of the same variable in CTA `rank`, and loads through it.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_map(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ float2 ld_cluster_f32x2(uint32_t addr) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void set_error(int* err, int bits) {
   if (err) atomicOr(err, bits);
 }

@@ -65,6 +65,11 @@ const char* dsa_last_error_message(void);
  *   merge_pdl          1 (default) launches the merge grid as a programmatic
  *                      dependent of the attention grid; 0 a plain launch
  *   indexer_tiles_per_cta  128-token tiles per indexer CTA (0: 16)
+ *   attention_cluster  2, 4 or 8: where (token, 16-head group) pairs x C
+ *                      CTAs fit on the GPU at once, each pair is split over a
+ *                      thread-block cluster of C CTAs that merge through
+ *                      distributed shared memory (one launch, no merge grid);
+ *                      0 or 1 (default): stream-K + merge grid
  * dsa_set_options(NULL) restores every default.  Changing options while
  * other host threads launch gives each launch either the old or the new set.
  */
@@ -76,6 +81,7 @@ typedef struct dsa_options {
   int attention_grids;
   int merge_pdl;
   int indexer_tiles_per_cta;
+  int attention_cluster;
 } dsa_options;
 int dsa_set_options(const dsa_options* options);
 int dsa_get_options(dsa_options* options);

@@ -155,3 +155,24 @@ def test_tvm_ffi_slot_registered_and_routes_to_kernel():
         f(torch.zeros(1, 16, 512, dtype=bf), torch.zeros(1, 16, 64, dtype=bf),
           torch.zeros(2, 64, 512, dtype=bf), torch.zeros(2, 64, 64, dtype=bf),
           torch.zeros(1, 2048, dtype=torch.int32), 0.1)
+
+
+def test_options_struct_round_trip_and_validation():
+    """dsa_set_options / dsa_get_options (host only): the ctypes struct has the
+    header's field count, values round-trip, out-of-range fields (a cluster
+    size other than 2, 4 or 8) are rejected and leave the options unchanged."""
+    hdr = open(os.path.join(ROOT, "include", "dsa_b200.h")).read()
+    body = re.search(r"typedef struct dsa_options \{(.*?)\} dsa_options;", hdr, re.S).group(1)
+    assert len(re.findall(r"\bint \w+;", body)) == len(_lib.Options._fields_)
+    lib = _lib.load()
+    lib.dsa_set_options.argtypes = [ctypes.POINTER(_lib.Options)]
+    lib.dsa_get_options.argtypes = [ctypes.POINTER(_lib.Options)]
+    try:
+        assert lib.dsa_set_options(ctypes.byref(_lib.Options(merge_pdl=1, attention_cluster=4))) == 0
+        got = _lib.Options()
+        assert lib.dsa_get_options(ctypes.byref(got)) == 0 and got.attention_cluster == 4
+        for bad in (3, -1, 16):
+            assert lib.dsa_set_options(ctypes.byref(_lib.Options(merge_pdl=1, attention_cluster=bad))) != 0
+        assert lib.dsa_get_options(ctypes.byref(got)) == 0 and got.attention_cluster == 4
+    finally:
+        lib.dsa_set_options(None)
