@@ -83,22 +83,30 @@ def indexer_scores(q_fp8, k_cache_fp8, k_scale, weights, seq_lens, block_table, 
     return out
 
 
-def topk_select(scores, seq_lens, block_table=None, topk=2048, order="score"):
+def topk_select(scores, seq_lens, block_table=None, topk=2048, order="score", out=None):
     """Exact top-k per row of `scores` [B, L] over the first seq_lens[b] entries
     (ties toward the lower position).  Returns (positions [B, topk] int32,
     slots [B, topk] int32 or None), -1 padded; order "score" emits descending
     score (ties by ascending position), "position" emits ascending position
-    (skips the sort)."""
+    (skips the sort).  out: optional (positions, slots) int32 [B, topk] row-major
+    tensors to write into (slots None when block_table is None)."""
     assert order in ("score", "position")
     assert scores.dtype == torch.float32 and scores.stride(-1) == 1 and scores.is_cuda
     B = scores.shape[0]
     seq_lens = seq_lens.to(torch.int32).contiguous()
-    pos = torch.empty((B, topk), dtype=torch.int32, device=scores.device)
-    slots = None
+    if out is not None:
+        pos, slots = out
+        for t in (pos, slots):
+            assert t is None or (t.dtype == torch.int32 and t.shape == (B, topk) and t.is_contiguous())
+        assert (slots is None) == (block_table is None)
+    else:
+        pos = torch.empty((B, topk), dtype=torch.int32, device=scores.device)
+        slots = None
     bt_ptr, bt_stride = None, 0
     if block_table is not None:
         block_table = block_table.to(torch.int32)
-        slots = torch.empty_like(pos)
+        if slots is None:
+            slots = torch.empty_like(pos)
         bt_ptr, bt_stride = block_table.data_ptr(), block_table.stride(0)
     with torch.cuda.device(scores.device):
         stream = torch.cuda.current_stream(scores.device).cuda_stream

@@ -85,11 +85,16 @@ def _check_inputs(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices):
 
 
 def kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, *, output=None,
-           lse=None):
+           lse=None, workspace=None):
     """DSA sparse attention; returns (output [T,H,512] bf16, lse [T,H] fp32 base-2).
 
     output/lse may be passed to write into existing tensors (same shapes);
     by default they are allocated, like the reference (kernel.py:156-157).
+    workspace: optional uint8 CUDA tensor of at least workspace_size(T, H,
+    topk) bytes, 256-byte aligned, zeroed before its first use (its first
+    word is the device error word); calls that may run concurrently (on
+    different streams) each need their own.  Default: the device's shared
+    workspace, so such calls must not overlap.
     """
     num_tokens, heads, num_pages, topk = _check_inputs(q_nope, q_pe, ckv_cache, kpe_cache,
                                                        sparse_indices)
@@ -105,8 +110,17 @@ def kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, *, outp
     _launch("dsa_sparse_attention", q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale,
             num_tokens, heads, num_pages, topk,
             (output.data_ptr(), output.stride(0), output.stride(1),
-             lse.data_ptr(), lse.stride(0), lse.stride(1)))
+             lse.data_ptr(), lse.stride(0), lse.stride(1)), workspace=workspace)
     return output, lse
+
+
+def workspace_size(num_tokens: int, heads: int = NUM_HEADS, topk: int = 2048, device=None) -> int:
+    """Bytes of the attention workspace a call of this shape needs on `device`
+    (default: the current device) under the current options."""
+    device = torch.device(device) if device is not None else torch.device(
+        "cuda", torch.cuda.current_device())
+    with torch.cuda.device(device):
+        return _workspace_bytes(device, num_tokens, heads, topk)
 
 
 _OPTION_FIELDS = [f for f, _ in _lib.Options._fields_]
@@ -158,7 +172,7 @@ def _workspace_bytes(device, num_tokens, heads, topk):
 
 
 def _launch(fn, q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, num_tokens, heads,
-            num_pages, topk, out_args):
+            num_pages, topk, out_args, workspace=None):
     if sparse_indices.dtype != torch.int32:
         sparse_indices = sparse_indices.to(torch.int32)
     if sparse_indices.stride(-1) != 1:
@@ -171,7 +185,13 @@ def _launch(fn, q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, nu
     with torch.cuda.device(device):
         stream = torch.cuda.current_stream(device)
         nbytes = _workspace_bytes(device, num_tokens, heads, topk)
-        ws = workspace_for(device).get(device, nbytes)
+        if workspace is not None:
+            if not (workspace.is_cuda and workspace.device == device and workspace.dtype == torch.uint8
+                    and workspace.is_contiguous()):
+                raise ValueError("workspace must be a contiguous uint8 tensor on the inputs' device")
+            ws = workspace  # the library checks its size and alignment
+        else:
+            ws = workspace_for(device).get(device, nbytes)
         _lib.call(
             fn,
             q_nope.data_ptr(), q_nope.stride(0), q_nope.stride(1),

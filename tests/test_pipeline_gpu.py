@@ -69,3 +69,25 @@ def test_cuda_graph_step(cuda_device):
     assert torch.equal(out2, eo2) and torch.equal(lse2, el2)
     assert not torch.equal(out2, eo)
     _ = out_bits
+
+
+def test_private_workspace_and_topk_out(cuda_device):
+    """kernel(workspace=) with a caller-owned workspace and topk_select(out=)
+    into caller-owned tensors give the same results as the defaults."""
+    from flashinfer_repo_b200 import indexer as IX
+    from flashinfer_repo_b200.kernel import kernel, workspace_size
+    ic, host, a = _setup(cuda_device, [3000, 1200, 4096])
+    scores = IX.indexer_scores(*a[:6])
+    pos, slots = IX.topk_select(scores, a[4], a[5], 2048, order="position")
+    pos2 = torch.empty_like(pos)
+    slots2 = torch.empty_like(slots)
+    IX.topk_select(scores, a[4], a[5], 2048, order="position", out=(pos2, slots2))
+    assert torch.equal(pos, pos2) and torch.equal(slots, slots2)
+    o1, l1 = kernel(*a[6:10], slots, W.SM_SCALE)
+    ws = torch.zeros(workspace_size(3, 16, 2048, cuda_device), dtype=torch.uint8, device=cuda_device)
+    o2, l2 = kernel(*a[6:10], slots, W.SM_SCALE, workspace=ws)
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2) and torch.equal(l1, l2)
+    assert int(ws[:4].view(torch.int32).item()) == 0  # the error word of this workspace
+    with pytest.raises(Exception):
+        kernel(*a[6:10], slots, W.SM_SCALE, workspace=ws[:64])  # too small: the library refuses
