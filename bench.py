@@ -225,6 +225,44 @@ def reference_run_fn():
     return mod.run, None
 
 
+def measure_reference_gpu(qn, qp, ckv, kpe, idx, scale, out, lse, flush, side, stream, steps):
+    """The reference's own GPU operators on this batch: the Triton `kernel`
+    (solution/triton/kernel.py:138-182) and `kernel_splitk` with SPLIT_K=16
+    (:496-567), imported unmodified from baseline/_ref, each captured in CUDA
+    graphs and timed exactly like this library's operator (graph nodes, L2
+    flushed before every step).  Also the largest difference of their results
+    from this library's (out, lse) on the full batch.  Returns a dict, or
+    {"unavailable": why}."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isfile(os.path.join(ref, "solution", "triton", "kernel.py")):
+        return {"unavailable": "baseline/_ref is missing (baseline/install_reference.py was not run)"}
+    try:
+        if ref not in sys.path:
+            sys.path.insert(0, ref)
+        import solution.triton.kernel as rk  # namespace package of the unmodified checkout
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"cannot import the reference kernels: {type(e).__name__}: {e}"}
+    T = idx.shape[0]
+    res = {"source": "baseline/_ref solution/triton/kernel.py (unmodified), CUDA graphs, L2 flushed per step",
+           "steps": steps}
+    variants = (("kernel", lambda: rk.kernel(qn, qp, ckv, kpe, idx, scale)),
+                ("kernel_splitk16", lambda: rk.kernel_splitk(qn, qp, ckv, kpe, idx, scale, SPLIT_K=16)))
+    for name, fn in variants:
+        try:
+            with torch.cuda.stream(side):
+                ro, rl = fn()  # compiles the Triton kernel outside any capture
+            torch.cuda.synchronize()
+            ms = statistics.median(graph_timed_steps(fn, steps, flush, side, stream))
+            d_out = (ro.float() - out.float()).abs()
+            fin = torch.isfinite(rl) & torch.isfinite(lse)
+            res[name] = {"ms_per_step": ms, "value": T / (ms / 1e3), "unit": UNIT,
+                         "max_abs_diff_out_vs_ours": float(torch.nan_to_num(d_out, nan=float("inf")).max()),
+                         "max_abs_diff_lse_vs_ours": float((rl - lse).abs()[fin].max()) if fin.any() else 0.0}
+        except Exception as e:  # noqa: BLE001
+            res[name] = {"unavailable": f"{type(e).__name__}: {e}"}
+    return res
+
+
 def reference_cpu_run(qn, qp, ckv, kpe, idx, scale, max_calls, budget_s=60.0, warmup=1):
     """Time the reference `run` on the host cores (torch CPU, all threads) on
     the full batch: one call = every token of the batch over the whole cache,
@@ -583,6 +621,14 @@ def run_ours(args):
     cfg3 = (measure_cfg3(dev, world, rank, min(args.steps, 20), args.warmup, dist)
             if world > 1 and not args.skip_extras else None)
 
+    ref_gpu = None
+    if world == 1 and not args.skip_extras:
+        with torch.cuda.stream(side):
+            kernel(qn, qp, ckv, kpe, idx, scale, output=out, lse=lse)
+        torch.cuda.synchronize()
+        ref_gpu = measure_reference_gpu(qn, qp, ckv, kpe, idx, scale, out, lse, flush, side, stream,
+                                        min(args.steps, 50))
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.skip_extras:
         os.sched_setaffinity(0, all_cpus)  # the CPU baseline uses every host core
@@ -634,6 +680,7 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "cfg4": cfg4,
             "cfg3": cfg3,
+            "reference_gpu": ref_gpu,
         }), flush=True)
     if dist:
         dist.destroy_process_group()
@@ -697,13 +744,31 @@ def measure_cfg4(dev, rank, steps, warmup, requests):
             ev[3].synchronize()
             parts += [ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]), ev[2].elapsed_time(ev[3])]
     parts /= steps
-    total = parts.sum()
+    # the whole step as one CUDA graph (indexer -> top-k -> attention, as a
+    # serving loop would capture it), timed the same way
+    from flashinfer_repo_b200.pipeline import DecodeStepGraph
+    step = DecodeStepGraph(d["q8"], d["k8"], d["scale"], d["w"], d["seq_lens"], d["block_table"],
+                           d["q_nope"], d["q_pe"], d["ckv"], d["kpe"], d["sm_scale"])
+    one = []
+    for i in range(warmup + steps):
+        flush(i)
+        torch.cuda._sleep(100_000)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        step.replay()
+        e1.record(stream)
+        e1.synchronize()
+        if i >= warmup:
+            one.append(e0.elapsed_time(e1))
+    total = statistics.median(one)
     ib = indexer_bytes(d["seq_lens"])
     ab = attention_bytes(slots)
     peak, kind = peaks()
     res = {
         "workload": f"cfg4: T={T} requests, ctx 32768, FP8 indexer 64x128, top-2048, 16-head MLA",
         "steps": steps, "value": T / (total / 1e3), "unit": UNIT, "ms_per_step": total,
+        "step": "one CUDA graph of the whole step (pipeline.DecodeStepGraph), median",
+        "ms_per_step_stage_sum": float(parts.sum()),
         "kernels_ms": {"indexer": parts[0], "topk": parts[1], "attention": parts[2]},
         "indexer_roofline": {"bound": "hbm", "kernel": "dsa_indexer_kernel", "alg_bytes": ib,
                              "achieved": ib / (parts[0] / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
@@ -714,7 +779,7 @@ def measure_cfg4(dev, rank, steps, warmup, requests):
         "gpu_launches_per_step": 4,  # indexer, top-k, attention, merge
         "clocks": clk.summary(),
     }
-    del d, scores, out, lse, box, graphs
+    del d, scores, out, lse, box, graphs, step
     torch.cuda.empty_cache()
     return res
 
