@@ -313,7 +313,40 @@ __global__ void __launch_bounds__(kTopkThreads)
       if (tid == 0) S.ncand = 0;
       __syncthreads();
       uint32_t n_gt = 0;
-      for (int gr = g0; gr < g1; gr += 32) {
+      if (cached) {
+        // keys in shared memory: four ballots (one per key of a lane's group)
+        // give every candidate of 128 keys its slot after one atomic, no scan
+        const uint32_t lt = (1u << lane) - 1u;
+#pragma unroll 2
+        for (int gr = g0; gr < g1; gr += 32) {
+          const int g = gr + lane;
+          const bool gin = g < g1;
+          const uint4 kk = gin ? S.keys[g] : make_uint4(0u, 0u, 0u, 0u);
+          const uint32_t v[4] = {kk.x, kk.y, kk.z, kk.w};
+          uint32_t bq[4], tot = 0;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const bool in = gin && 4 * g + q < len;
+            n_gt += (in && v[q] > hi) ? 1u : 0u;
+            bq[q] = __ballot_sync(0xffffffffu, in && v[q] >= lo && v[q] <= hi);
+            tot += (uint32_t)__popc(bq[q]);
+          }
+          if (tot) {
+            uint32_t base = 0;
+            if (lane == 0) base = atomicAdd(&S.ncand, tot);
+            base = __shfl_sync(0xffffffffu, base, 0);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              if ((bq[q] >> lane) & 1u) {
+                const uint32_t o = base + (uint32_t)__popc(bq[q] & lt);
+                if (o < kMaxCand) cand[o] = ((unsigned long long)v[q] << 32) | (uint32_t)(4 * g + q);
+              }
+              base += (uint32_t)__popc(bq[q]);
+            }
+          }
+        }
+      }
+      for (int gr = cached ? g1 : g0; gr < g1; gr += 32) {
         const int g = gr + lane;
         const uint4 kk = g < g1 ? group_at(g) : make_uint4(0u, 0u, 0u, 0u);
         const uint32_t v[4] = {kk.x, kk.y, kk.z, kk.w};
@@ -432,7 +465,35 @@ __global__ void __launch_bounds__(kTopkThreads)
     S.w_eqb[lane] = eb;
   }
   __syncthreads();
-  {
+  if (cached) {
+    // keys in shared memory, one per lane per step: ballots of (key > T) and
+    // (key == T) give each taken key its rank in position order; equal keys
+    // (rare) are taken while their rank among this row's equal keys is below
+    // need.  Unrolled so that several steps' shared-memory loads are in flight.
+    uint32_t off = S.w_off[warp], eq_rank = S.w_eqb[warp];
+    const uint32_t* K1 = reinterpret_cast<const uint32_t*>(S.keys);
+    const int i1 = min(len, 4 * g1);
+    const uint32_t lt = (1u << lane) - 1u;
+#pragma unroll 4
+    for (int i = 4 * g0 + lane; i - lane < i1; i += 32) {
+      const bool in = i < i1;
+      const uint32_t v = in ? K1[i] : 0u;
+      bool take = in && (all || v > T);
+      const bool eq = in && !all && v == T;
+      const uint32_t be = __ballot_sync(0xffffffffu, eq);
+      if (be) {  // uniform over the warp
+        const uint32_t room = (uint32_t)need > eq_rank ? (uint32_t)need - eq_rank : 0u;
+        take = take || (eq && (uint32_t)__popc(be & lt) < room);
+        eq_rank += (uint32_t)__popc(be);
+      }
+      const uint32_t bt = __ballot_sync(0xffffffffu, take);
+      if (take) {
+        const uint32_t w = off + (uint32_t)__popc(bt & lt);
+        if (w < (uint32_t)kTopkMax) S.buf[w] = ((unsigned long long)v << 32) | (0xFFFFFFFFu - (uint32_t)i);
+      }
+      off += (uint32_t)__popc(bt);
+    }
+  } else {
     uint32_t off = S.w_off[warp], eq_rank = S.w_eqb[warp];
     for (int gr = g0; gr < g1; gr += 32) {
       const int g = gr + lane;
