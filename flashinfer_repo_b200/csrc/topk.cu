@@ -55,6 +55,7 @@ __device__ __forceinline__ uint32_t ordered_key(float x) {
 //    lower position): strides below 64 in registers with warp shuffles,
 //    larger ones in shared memory.
 constexpr int kHistCopies = 8;
+constexpr int kFixedShift = 21;  // fixed first-pass bins: key >> 21 (2048 bins)
 constexpr int kKeyCache = 32768;
 
 struct TopkSmem {
@@ -164,7 +165,13 @@ __global__ void __launch_bounds__(kTopkThreads)
     return r;
   };
 
-  // ---- 1. load and key range
+  // ---- 1. load and key range; rows held in shared memory also get the first
+  // histogram here, on fixed bins (the top 11 bits of the key)
+  const bool fuse = cached && len > k;
+  if (fuse) {
+    for (int j = tid; j < kHistCopies * kBins; j += kTopkThreads) (&S.hist[0][0])[j] = 0;
+    __syncthreads();
+  }
   uint32_t tlo = 0xffffffffu, thi = 0u;
   auto fold = [&](uint32_t key, int i) {
     if (i < len) {
@@ -195,6 +202,13 @@ __global__ void __launch_bounds__(kTopkThreads)
           fold(kk.y, i + 1);
           fold(kk.z, i + 2);
           fold(kk.w, i + 3);
+          if (fuse) {
+            uint32_t* mine = S.hist[warp & (kHistCopies - 1)];
+            atomicAdd(&mine[kk.x >> kFixedShift], 1u);
+            if (i + 1 < len) atomicAdd(&mine[kk.y >> kFixedShift], 1u);
+            if (i + 2 < len) atomicAdd(&mine[kk.z >> kFixedShift], 1u);
+            if (i + 3 < len) atomicAdd(&mine[kk.w >> kFixedShift], 1u);
+          }
         }
       }
     }
@@ -284,27 +298,39 @@ __global__ void __launch_bounds__(kTopkThreads)
   if (!all) {
     uint32_t* hist0 = &S.hist[0][0];
     uint32_t* mine = S.hist[warp & (kHistCopies - 1)];
+    bool fused = fuse;  // the first histogram came with the load
     while (lo != hi) {
-      const int shift = bin_shift(hi - lo);
-      const int nb = (int)((hi - lo) >> shift) + 1;
-      for (int j = tid; j < kHistCopies * kBins; j += kTopkThreads) hist0[j] = 0;
-      __syncthreads();
-      for (int g = tid; g < n4; g += kTopkThreads) {
-        const uint4 kk = group_at(g);
-        const int i = 4 * g;
-        if (kk.x >= lo && kk.x <= hi) atomicAdd(&mine[(kk.x - lo) >> shift], 1u);
-        if (i + 1 < len && kk.y >= lo && kk.y <= hi) atomicAdd(&mine[(kk.y - lo) >> shift], 1u);
-        if (i + 2 < len && kk.z >= lo && kk.z <= hi) atomicAdd(&mine[(kk.z - lo) >> shift], 1u);
-        if (i + 3 < len && kk.w >= lo && kk.w <= hi) atomicAdd(&mine[(kk.w - lo) >> shift], 1u);
+      uint32_t kept;
+      if (fused) {
+        fused = false;
+        find_bin(hist0, kHistCopies, kBins, kBins, need);
+        const uint32_t d = S.bstar;
+        kept = S.bcount;
+        need -= (int)S.above;
+        lo = max(lo, d << kFixedShift);
+        hi = min(hi, (d << kFixedShift) | ((1u << kFixedShift) - 1u));
+      } else {
+        const int shift = bin_shift(hi - lo);
+        const int nb = (int)((hi - lo) >> shift) + 1;
+        for (int j = tid; j < kHistCopies * kBins; j += kTopkThreads) hist0[j] = 0;
+        __syncthreads();
+        for (int g = tid; g < n4; g += kTopkThreads) {
+          const uint4 kk = group_at(g);
+          const int i = 4 * g;
+          if (kk.x >= lo && kk.x <= hi) atomicAdd(&mine[(kk.x - lo) >> shift], 1u);
+          if (i + 1 < len && kk.y >= lo && kk.y <= hi) atomicAdd(&mine[(kk.y - lo) >> shift], 1u);
+          if (i + 2 < len && kk.z >= lo && kk.z <= hi) atomicAdd(&mine[(kk.z - lo) >> shift], 1u);
+          if (i + 3 < len && kk.w >= lo && kk.w <= hi) atomicAdd(&mine[(kk.w - lo) >> shift], 1u);
+        }
+        __syncthreads();
+        find_bin(hist0, kHistCopies, kBins, nb, need);
+        const uint32_t d = S.bstar;
+        kept = S.bcount;
+        need -= (int)S.above;
+        const uint32_t nlo = lo + (d << shift);
+        hi = (uint32_t)min((unsigned long long)hi, (unsigned long long)nlo + (1ull << shift) - 1ull);
+        lo = nlo;
       }
-      __syncthreads();
-      find_bin(hist0, kHistCopies, kBins, nb, need);
-      const uint32_t d = S.bstar;
-      const uint32_t kept = S.bcount;
-      need -= (int)S.above;
-      const uint32_t nlo = lo + (d << shift);
-      hi = (uint32_t)min((unsigned long long)hi, (unsigned long long)nlo + (1ull << shift) - 1ull);
-      lo = nlo;
       __syncthreads();  // S.bstar / S.above / the histograms are rewritten next
       if (kept > kMaxCand) continue;  // another full pass narrows the bin first
       // ---- candidate pass over this warp's groups: keys > hi are taken,

@@ -179,6 +179,27 @@ def test_causal_prefill_against_oracle(cuda_device):
     assert_attention_close(out, lse, ref_out, ref_lse, "prefill")
 
 
+def test_full_size_cfg5_subsample_against_oracle(cuda_device):
+    """BASELINE cfg5 at full size: 4096 causal queries over one 65536-token
+    sequence, the whole grid launched as in the bench (tokens outnumber CTAs:
+    boundary-row merge plan); 40 tokens spread over the batch (the first and
+    last, CTA-boundary neighbourhoods included by the spread) are checked
+    against the oracle, plus the -inf-free LSE of every token."""
+    from flashinfer_repo_b200.bench_inputs import make_prefill_device
+    qn, qp, ckv, kpe, idx, scale = make_prefill_device(seed=6, device=cuda_device)
+    out, lse = kernel(qn, qp, ckv, kpe, idx, scale)
+    torch.cuda.synchronize()
+    assert read_device_error(cuda_device) == 0
+    T = idx.shape[0]
+    assert T == 4096 and torch.isfinite(lse).all()
+    sel = np.unique(np.concatenate([[0, 1, T - 2, T - 1],
+                                    np.random.default_rng(6).choice(T, 36, replace=False)]))
+    st = torch.from_numpy(sel).to(cuda_device)
+    ref_out, ref_lse = O.dsa_attention(out_bits(qn[st]), out_bits(qp[st]), out_bits(ckv), out_bits(kpe),
+                                       idx[st].cpu().numpy(), scale)
+    assert_attention_close(out[st], lse[st], ref_out, ref_lse, "cfg5 full, subsample")
+
+
 def test_tvm_ffi_entry_point(cuda_device):
     """Called through the TVM-FFI global `flashinfer.kernel` (the reference's
     CUDA binding slot), the operator returns the same result."""
