@@ -6,7 +6,7 @@ plus the FP8 lightning indexer and exact top-k that feed it.  All compute runs
 in libdsa_b200.so (hand-written CUDA for sm_100a, C ABI in include/dsa_b200.h).
 """
 from .kernel import (get_options, kernel, kernel_splitk, kernel_splitk_v2, options,  # noqa: F401
-                     read_device_error, set_options)
+                     read_device_error, set_options, workspace_size)
 
 __all__ = ["kernel", "kernel_splitk", "kernel_splitk_v2", "read_device_error", "options",
-           "set_options", "get_options"]
+           "set_options", "get_options", "workspace_size"]
