@@ -71,6 +71,11 @@ struct AttnParams {
   int tiles_per_token;  // topk / 32
   float scale_log2;     // sm_scale * log2(e)
   int tiles_base, tiles_rem;
+  // Token-aligned plan when > 0: every virtual token is split over exactly
+  // `per_token` CTAs, part j of a token taking its tiles
+  // [j*tpt/per_token, (j+1)*tpt/per_token) (integer division); tiles_base /
+  // tiles_rem are then unused.  0: the flat split of all tiles above.
+  int per_token;
   // Optional extra output targets (fused all-gather of head-sharded outputs):
   // when n_peers > 0, every output / lse store goes to each of the n_peers
   // bases (peer GPUs' buffers over NVLink, this rank's head slice), with the
@@ -114,9 +119,17 @@ struct AttnSmem {
 static_assert(kClPartFloats * 4 <= 2 * kRows * kCkvStride, "cluster partial must fit in two ckv stages");
 
 __device__ __forceinline__ int cta_start(const AttnParams& p, int c) {
+  if (p.per_token > 0) {
+    const int v = c / p.per_token, j = c - v * p.per_token;
+    return v * p.tiles_per_token + (j * p.tiles_per_token) / p.per_token;
+  }
   return c * p.tiles_base + min(c, p.tiles_rem);
 }
 __device__ __forceinline__ int cta_of_tile(const AttnParams& p, int tile) {
+  if (p.per_token > 0) {  // the part j with j*tpt/C <= r < (j+1)*tpt/C
+    const int v = tile / p.tiles_per_token, r = tile - v * p.tiles_per_token;
+    return v * p.per_token + ((r + 1) * p.per_token - 1) / p.tiles_per_token;
+  }
   const int big = (p.tiles_base + 1) * p.tiles_rem;
   return tile < big ? tile / (p.tiles_base + 1) : p.tiles_rem + (tile - big) / p.tiles_base;
 }
@@ -1154,6 +1167,7 @@ int device_slots(int nst, int* sms_out) {
 
 struct Plan {
   int ctas, base, rem;
+  int per_token;  // token-aligned plan: CTAs per virtual token, 0 otherwise
   int cluster;  // CTAs per token in the cluster plan, 0 otherwise
   int64_t vtokens, total_tiles;
   size_t part_off, bytes;
@@ -1203,17 +1217,26 @@ int make_plan(int64_t num_tokens, int64_t heads, int64_t topk, int nst, Plan* pl
   ctas = std::min<int64_t>(ctas, (pl->total_tiles + min_tiles - 1) / min_tiles);
   if (ctas < 1) ctas = 1;
   // Token-aligned split: when there are fewer (token, head group) pairs than
-  // resident CTAs, give every pair the same number C of CTAs (C the largest
-  // divisor of its tile count that fits), so no CTA straddles two pairs and
-  // each pair has exactly C partials -- used when that fills >= 80% of the
-  // slots.  Measured on a B200 (400-step means): cfg2 T=64 42.49 -> 41.53 us
-  // (256 CTAs), T=32 30.77 -> 28.60, a 64-head cfg3 shard 28.6 -> 25.6,
-  // T=128 and 128 heads equal.
+  // resident CTAs, every pair gets the same number C of CTAs, so no CTA
+  // straddles two pairs and each pair has exactly C partials.  C is the
+  // largest divisor of the pair's tile count that fits (the flat split above
+  // then yields this partition) when that fills >= 80% of the slots; else
+  // C = floor(slots / pairs) when C >= 4 and it fills >= 80% (part j of a pair
+  // takes tiles [j*tpt/C, (j+1)*tpt/C)); else stream-K.  Measured on B200s
+  // (300-400-step means, same process): T=64 (C=4) 42.0 vs 43.1 us stream-K;
+  // T=24 (C=12) 26.8 vs 28.5; T=48 (C=6) 34.8 vs 36.8; 48/64-head cfg3 shards
+  // 2 us faster; C=3 (T=80) lost 1 us; the per-token closed form costs ~1 us
+  // more than the flat one for the same partition, so divisors come first.
+  pl->per_token = 0;
   if (!tc && o.attention_ctas == 0 && pl->vtokens < slots) {
-    for (int64_t c = std::min<int64_t>(tpt / min_tiles, slots / pl->vtokens); c >= 2; --c) {
-      if (tpt % c) continue;
-      if (pl->vtokens * c * 10 >= slots * 8) ctas = pl->vtokens * c;
-      break;
+    const int64_t cmax = std::min<int64_t>(tpt / min_tiles, slots / pl->vtokens);
+    int64_t cd = cmax;
+    while (cd >= 2 && tpt % cd) --cd;
+    if (cd >= 2 && pl->vtokens * cd * 10 >= slots * 8) {
+      ctas = pl->vtokens * cd;
+    } else if (cmax >= 4 && pl->vtokens * cmax * 10 >= slots * 8) {
+      ctas = pl->vtokens * cmax;
+      pl->per_token = (int)cmax;
     }
   }
   pl->cluster = 0;
@@ -1222,6 +1245,7 @@ int make_plan(int64_t num_tokens, int64_t heads, int64_t topk, int nst, Plan* pl
     const int64_t n = pl->vtokens * c;
     if (tpt % c == 0 && tpt / c >= min_tiles && n <= slots && pl->vtokens <= resident_clusters(nst, c)) {
       pl->cluster = c;
+      pl->per_token = 0;
       ctas = n;
     }
   }
@@ -1401,6 +1425,7 @@ static int attention_impl(const void* q_nope, int64_t q_nope_stride_token, int64
   p.scale_log2 = sm_scale * 1.4426950408889634f;
   p.tiles_base = pl.base;
   p.tiles_rem = pl.rem;
+  p.per_token = pl.per_token;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   p.err = reinterpret_cast<int*>(ws);
   p.part = reinterpret_cast<float*>(ws + pl.part_off);

@@ -72,6 +72,23 @@ def test_more_tokens_than_ctas(cuda_device, ctas):
         _oracle_check(case, cuda_device)
 
 
+@pytest.mark.parametrize("T", [37, 48, 64, 100])
+def test_token_aligned_plans(cuda_device, T):
+    """Batches with fewer tokens than resident CTAs: each token split over the
+    same number of CTAs, also when that number does not divide its 64 tiles
+    (T=37: 8 CTAs per token, T=48: 6), or the stream-K plan (T=100), agree
+    with the oracle and with an explicit stream-K partition."""
+    ctx = np.random.default_rng(T).integers(300, 5000, size=T)
+    case = W.make_attention_case(300 + T, ctx)
+    _, out, lse = _oracle_check(case, cuda_device)
+    with options(attention_ctas=296):
+        o2, l2 = kernel(*case_to_device(case, cuda_device), case.sm_scale)
+    torch.cuda.synchronize()
+    assert (out.float() - o2.float()).abs().max().item() <= 2 ** -6
+    assert torch.allclose(lse, l2, atol=1e-5, rtol=0)
+    assert read_device_error(cuda_device) == 0
+
+
 @pytest.mark.parametrize("stages", [2, 3, 4])
 def test_pipeline_depths(cuda_device, stages):
     case = W.make_attention_case(8, [5000, 2100, 4096])
