@@ -64,7 +64,7 @@ const char* dsa_last_error_message(void);
  *                      written), 2 the merge grid alone; 0 both
  *   merge_pdl          1 (default) launches the merge grid as a programmatic
  *                      dependent of the attention grid; 0 a plain launch
- *   indexer_tiles_per_cta  128-token tiles per indexer CTA (0: 16)
+ *   indexer_tiles_per_cta  128-token tiles per indexer CTA (0: 20)
  *   attention_cluster  2, 4 or 8: where (token, 16-head group) pairs x C
  *                      CTAs fit on the GPU at once, each pair is split over a
  *                      thread-block cluster of C CTAs that merge through
