@@ -391,6 +391,37 @@ def copy_bandwidth(dev, nbytes=64 << 20, reps=5):
     return out
 
 
+def copy_floor_ms(dev, uploads, downloads, steps=200):
+    """Per-step time of the e2e pipeline's own copies alone (its pinned and
+    device buffers, the same copy calls), the upload on one stream and the
+    downloads on another at once, no kernels: the directions contend on the
+    host link, so this, not either bandwidth alone, is the floor the e2e
+    pipeline can reach on this machine.  uploads / downloads: per buffer set,
+    a list of (dst, src) pairs."""
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    st = torch.cuda.current_stream(dev)
+    nb = len(uploads)
+    res = []
+    for _ in range(2):  # the first round warms the copy path
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        up.wait_stream(st)
+        down.wait_stream(st)
+        for i in range(steps):
+            with torch.cuda.stream(up):
+                for dst, src in uploads[i % nb]:
+                    dst.copy_(src, non_blocking=True)
+            with torch.cuda.stream(down):
+                for dst, src in downloads[i % nb]:
+                    dst.copy_(src, non_blocking=True)
+        st.wait_stream(up)
+        st.wait_stream(down)
+        e1.record(st)
+        e1.synchronize()
+        res.append(e0.elapsed_time(e1) / steps)
+    return res[-1]
+
+
 def run_ours(args):
     rank, world, local = dist_setup(args.gpus)
     torch.cuda.set_device(local)
@@ -617,6 +648,8 @@ def run_ours(args):
     peak, peak_kind = peaks()
 
     copies = copy_bandwidth(dev)
+    floor_ms = copy_floor_ms(dev, [[(dstage[b_], host[b_])] for b_ in range(NB)],
+                             [[(h_out[b_], d_out[b_]), (h_lse[b_], d_lse[b_])] for b_ in range(NB)])
     cfg4 = None if args.skip_extras else measure_cfg4(dev, rank, min(args.steps, 20), args.warmup, 128)
     cfg3 = (measure_cfg3(dev, world, rank, min(args.steps, 20), args.warmup, dist)
             if world > 1 and not args.skip_extras else None)
@@ -666,6 +699,7 @@ def run_ours(args):
                     "host_driven_ms_per_step": e2e_a / args.steps,
                     "one_graph_ms_per_step": e2e_b / args.steps,
                     "pcie_floor_ms_per_step": h2d / (copies["h2d_gbs"] * 1e9) * 1e3,
+                    "copy_floor_ms_per_step": floor_ms,
                     "copy_bandwidth_gbs": copies,
                     "note": "kernel() with pinned host buffers: per step the upload of q_nope, "
                             "q_pe and sparse_indices (one staging buffer, one copy), the operator, "
@@ -674,7 +708,9 @@ def run_ours(args):
                             "by the host per step or as 40 steps in one multi-stream CUDA graph (the "
                             "faster is the value), alternating two batches (inputs "
                             "larger than L2); pcie_floor = upload bytes at the pinned host-to-device "
-                            "bandwidth measured on this machine (copy_bandwidth_gbs)"},
+                            "bandwidth measured on this machine (copy_bandwidth_gbs); copy_floor = the "
+                            "same per-step upload and download run alone on two streams at once, "
+                            "measured here (the directions contend on the host link)"},
             "gpu_launches": 2 * args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,
