@@ -514,10 +514,14 @@ def run_ours(args):
     host = [host_in[b_ % 2][0] for b_ in range(NB)]
     dstage = [torch.empty(h.numel(), dtype=torch.uint8, device=dev) for h in host]
     dbuf = [views(dstage[b_], host_in[b_ % 2][1], host_in[b_ % 2][2]) for b_ in range(NB)]
-    h_out = [torch.empty(out.shape, dtype=out.dtype).pin_memory() for _ in range(NB)]
-    h_lse = [torch.empty(lse.shape, dtype=lse.dtype).pin_memory() for _ in range(NB)]
-    d_out = [torch.empty_like(out) for _ in range(NB)]
-    d_lse = [torch.empty_like(lse) for _ in range(NB)]
+    # a step's results likewise: output and LSE are typed views of one device
+    # buffer, downloaded with one copy into one pinned buffer
+    res_ts = (out, lse)
+    res_offs, res_bytes = layout(res_ts)
+    h_res = [torch.empty(res_bytes, dtype=torch.uint8).pin_memory() for _ in range(NB)]
+    d_res = [torch.empty(res_bytes, dtype=torch.uint8, device=dev) for _ in range(NB)]
+    h_out, h_lse = zip(*[views(h, res_ts, res_offs) for h in h_res])
+    d_out, d_lse = zip(*[views(d, res_ts, res_offs) for d in d_res])
     h2d = host[0].numel()
     d2h = h_out[0].numel() * 2 + h_lse[0].numel() * 4
     up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
@@ -531,8 +535,7 @@ def run_ours(args):
                lse=d_lse[b_])
 
     def part_down(b_):
-        h_out[b_].copy_(d_out[b_], non_blocking=True)
-        h_lse[b_].copy_(d_lse[b_], non_blocking=True)
+        h_res[b_].copy_(d_res[b_], non_blocking=True)
     cap = torch.cuda.Stream(dev)
     cap.wait_stream(stream)
     g_parts = []
@@ -649,7 +652,7 @@ def run_ours(args):
 
     copies = copy_bandwidth(dev)
     floor_ms = copy_floor_ms(dev, [[(dstage[b_], host[b_])] for b_ in range(NB)],
-                             [[(h_out[b_], d_out[b_]), (h_lse[b_], d_lse[b_])] for b_ in range(NB)])
+                             [[(h_res[b_], d_res[b_])] for b_ in range(NB)])
     cfg4 = None if args.skip_extras else measure_cfg4(dev, rank, min(args.steps, 20), args.warmup, 128)
     cfg3 = (measure_cfg3(dev, world, rank, min(args.steps, 20), args.warmup, dist)
             if world > 1 and not args.skip_extras else None)
@@ -704,7 +707,7 @@ def run_ours(args):
                     "note": "kernel() with pinned host buffers: per step the upload of q_nope, "
                             "q_pe and sparse_indices (one staging buffer, one copy), the operator, "
                             "and the download of output + "
-                            "LSE, pipelined over upload/compute/download streams (4 buffer sets), driven "
+                            "LSE (one buffer, one copy), pipelined over upload/compute/download streams (4 buffer sets), driven "
                             "by the host per step or as 40 steps in one multi-stream CUDA graph (the "
                             "faster is the value), alternating two batches (inputs "
                             "larger than L2); pcie_floor = upload bytes at the pinned host-to-device "
